@@ -1,0 +1,163 @@
+/*
+ * lightning_router.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream, is
+ * stream-ordered, never allocates or frees device memory (scratch is passed in
+ * as a workspace whose size is reported by a *_workspace_bytes query), and
+ * returns 0 on success or a negative LR_* status (see lr_status_string).
+ * Device-detected contract violations (an expert id out of range, a pipeline
+ * wait that ran out of time) are OR-ed into the optional `err` word, which the
+ * caller reads back when it chooses.
+ *
+ * Each entry point names the reference (AlexanderLeonida/LLM-Serving-Kernel-
+ * Optimization) interface it replaces.
+ */
+#ifndef LIGHTNING_ROUTER_H
+#define LIGHTNING_ROUTER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* lr_stream_t; /* == cudaStream_t */
+
+/* ---- status ------------------------------------------------------------ */
+#define LR_OK 0
+#define LR_ERR_INVALID_ARGUMENT (-1)
+#define LR_ERR_UNSUPPORTED (-2)
+#define LR_ERR_CUDA (-3)
+#define LR_ERR_WORKSPACE (-4)
+#define LR_ERR_NO_DEVICE (-5)
+
+/* bits OR-ed into the device `err` word */
+#define LR_DEVERR_BAD_EXPERT 0x1     /* an expert id outside [0, E) */
+#define LR_DEVERR_BAD_TOKEN 0x2      /* a source token outside [0, T) */
+#define LR_DEVERR_PIPE_TIMEOUT 0x4   /* a GEMM pipeline wait ran out of time */
+#define LR_DEVERR_BAD_SEGMENT 0x8    /* a GEMM row segment outside the row range */
+
+const char* lr_status_string(int status);
+int lr_abi_version(void);
+/* Last CUDA runtime error seen by an entry point on this thread (0 if none). */
+int lr_last_cuda_error(void);
+
+/* ---- gate projection --------------------------------------------------- */
+/* logits[T,E] (fp32) = h[T,d] (fp16) . wg[E,d]^T (fp16) (+ bias[E] fp32).
+ * Replaces TopKGating.gate_proj, lightning_router/models/gating.py:46,69.
+ * Limits: d % 16 == 0, 1 <= E <= 256.                                      */
+int lr_gate_logits(const void* h, const void* wg, const float* bias, int T, int d, int E,
+                   float* logits, lr_stream_t stream);
+
+/* ---- gating + dispatch -------------------------------------------------- */
+size_t lr_route_workspace_bytes(int num_tokens, int top_k, int num_experts);
+
+/* Fused top-k softmax gating and capacity-masked dispatch from fp32 logits.
+ * Replaces TopKGating.forward (lightning_router/models/gating.py:48-101)
+ * followed by expert_routing_forward (lightning_router/kernels/expert_routing.py:164-230).
+ * Slot s = t*k + j, j in descending-logit order (ties: lowest expert index).
+ * Outputs (S = T*k):
+ *   expert_ids[S] int32, gate_weights[S] fp32, token_indices[S] int32 (nullable),
+ *   offsets[E+1] int32 (UNCAPPED CSR, as the reference), kept_counts[E] int32,
+ *   aux_loss[1] fp32 (nullable; Switch load-balancing loss, gating.py:91-99),
+ *   permuted[S,d] fp16 (nullable => routing only), routing_w[S] fp32,
+ *   source_idx[S] int32, slot_pos[S] int32 (row of each slot or -1 if dropped).
+ * Rows of expert e occupy [offsets[e], offsets[e+1]); the first kept_counts[e]
+ * are its kept slots in slot order.  A dropped slot's row has routing_w = 0,
+ * source_idx = its token and (if fill_dropped) zeros.
+ * Limits: E <= 64, 1 <= k <= min(E, 8), d % 8 == 0.                        */
+int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, int E, int k,
+                            int capacity, float load_balance_weight, int fill_dropped,
+                            int32_t* expert_ids, float* gate_weights, int32_t* token_indices,
+                            int32_t* offsets, int32_t* kept_counts, float* aux_loss,
+                            void* permuted, float* routing_w, int32_t* source_idx,
+                            int32_t* slot_pos, void* workspace, size_t workspace_bytes,
+                            int32_t* err, lr_stream_t stream);
+
+size_t lr_dispatch_workspace_bytes(int num_slots, int num_experts);
+
+/* Dispatch of precomputed slots (expert id, gate weight, source token per slot).
+ * Replaces expert_routing_forward, lightning_router/kernels/expert_routing.py:164-230.
+ * Same output layout as lr_topk_gating_dispatch.  Limits: E <= 1024, d % 8 == 0. */
+int lr_expert_routing_forward(const void* tokens, const int32_t* expert_ids,
+                              const float* gate_weights, const int32_t* token_indices,
+                              int T, int d, int S, int E, int capacity, int fill_dropped,
+                              void* permuted, int32_t* offsets, float* routing_w,
+                              int32_t* source_idx, int32_t* kept_counts, int32_t* slot_pos,
+                              void* workspace, size_t workspace_bytes, int32_t* err,
+                              lr_stream_t stream);
+
+/* ---- combine ------------------------------------------------------------- */
+/* out[t,:] = fp16( sum_j gate_weights[t*k+j] * y[slot_pos[t*k+j], :] ) over kept
+ * slots, fp32 accumulation in slot order, one store per element, no atomics.
+ * Replaces the gather of lightning_router/kernels/expert_routing.py:238-298 on
+ * the layer path (lightning_router/models/moe_layer.py:126).  d % 8 == 0.  */
+int lr_combine(const void* y, const float* gate_weights, const int32_t* slot_pos,
+               int T, int k, int d, void* out, lr_stream_t stream);
+
+size_t lr_gather_workspace_bytes(int num_rows, int num_tokens);
+
+/* Row-wise weighted gather back to token order for arbitrary (rows -> token)
+ * maps: out[src[r]] += w[r] * y[r] over rows with w[r] != 0, fp32 accumulation
+ * in ascending row order per token, one fp16 store per element.
+ * Replaces expert_routing_gather, lightning_router/kernels/expert_routing.py:274-298. */
+int lr_expert_routing_gather(const void* y, const float* routing_w, const int32_t* source_idx,
+                             int R, int d, int T, void* out, void* workspace,
+                             size_t workspace_bytes, int32_t* err, lr_stream_t stream);
+
+/* ---- W4A16 GEMM -------------------------------------------------------- */
+/* Packed INT4 format (lightning_router/quantization/pack_weights.py:23-130):
+ * qweight (K, N/8) int32, nibble i of word j = column 8j+i; scales (K/g, N)
+ * fp16; zeros (K/g, N/8) int32 packed like qweight; w = fp16(scale*(q-zero)). */
+
+#define LR_FFN_MODE_PLAIN 0   /* C = A . W                                   */
+#define LR_FFN_MODE_SILU 1    /* C = silu(A . W)                             */
+#define LR_FFN_MODE_SWIGLU 2  /* C = silu(A . Wgate) * (A . Wup)             */
+
+/* One expert's matrices: index 0 gate, 1 up, 2 down (gate unused when not gated). */
+typedef struct lr_expert_weights {
+  const int32_t* qweight[3];
+  const void* scales[3];
+  const int32_t* zeros[3];
+} lr_expert_weights;
+
+/* Host-side encoding of the per-expert weight table (TMA descriptors and
+ * pointers).  Writes `lr_weight_table_bytes(E)` bytes into `host_table`
+ * (64-byte aligned host memory); the caller copies it to a 64-byte aligned
+ * device buffer once per weight set.  No CUDA calls besides descriptor encoding. */
+size_t lr_weight_table_bytes(int num_experts);
+int lr_encode_weight_table(const lr_expert_weights* experts, int E, int d_model, int d_ff,
+                           int group_size, int gated, void* host_table, size_t table_bytes);
+
+size_t lr_grouped_gemm_workspace_bytes(int num_experts);
+
+/* Grouped W4A16 GEMM on tcgen05 (swap-AB: weights are the 128-row UMMA M
+ * operand, tokens the N operand).  For each expert e, rows
+ * [seg_start[e], seg_start[e] + seg_len[e]) of A (R x K fp16, row-major)
+ * are multiplied with matrix `mat` (or gate/up for SWIGLU) of expert e and
+ * written to the same rows of C (R x N_out fp16).  seg_* live on the device.
+ * `max_rows_per_expert` bounds seg_len (selects the token tile); seg_len
+ * beyond it is clamped and flagged.
+ * Replaces ExpertGroup.forward / ExpertFFN._qmatmul + quantized_matmul
+ * (lightning_router/models/experts.py:58-121, kernels/quantized_matmul.py:122-173). */
+int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, int mat,
+                          const void* A, int R, int K, int N,
+                          const int32_t* seg_start, const int32_t* seg_len,
+                          int max_rows_per_expert, void* C, void* workspace,
+                          size_t workspace_bytes, int32_t* err, lr_stream_t stream);
+
+/* Single W4A16 GEMM C[M,N] = A[M,K] . dequant(qweight) (fp16 out).
+ * Replaces quantized_matmul, lightning_router/kernels/quantized_matmul.py:122-173.
+ * `device_table` holds one expert entry encoded with gated = 0 whose matrix 2
+ * is (qweight, scales, zeros) with K = d_ff, N = d_model.                     */
+int lr_quantized_matmul(const void* device_table, const void* A, int M, int K, int N,
+                        void* C, void* workspace, size_t workspace_bytes, int32_t* err,
+                        lr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIGHTNING_ROUTER_H */

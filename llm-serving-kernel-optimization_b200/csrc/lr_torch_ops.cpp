@@ -1,0 +1,306 @@
+// lr_torch_ops.cpp -- registers the C-ABI entry points of liblr_kernels.so as
+// torch custom ops (namespace `lightning_router`).  Tensors are validated here,
+// outputs and workspaces come from the caching allocator on the current
+// stream, and a non-zero LR_* status raises a RuntimeError.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstring>
+#include <tuple>
+#include <vector>
+
+#include "../../include/lightning_router.h"
+
+namespace {
+
+void check_status(int rc, const char* what) {
+  TORCH_CHECK(rc == LR_OK, "lightning_router.", what, " failed: ", lr_status_string(rc), " (",
+              rc, ")");
+}
+
+lr_stream_t cur_stream() {
+  return reinterpret_cast<lr_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+int32_t* err_ptr(const c10::optional<at::Tensor>& err) {
+  if (!err.has_value() || !err->defined()) return nullptr;
+  TORCH_CHECK(err->is_cuda() && err->scalar_type() == at::kInt && err->numel() >= 1,
+              "err must be a CUDA int32 tensor");
+  return err->data_ptr<int32_t>();
+}
+
+at::Tensor workspace(size_t bytes, const at::Tensor& like) {
+  return at::empty({static_cast<int64_t>(bytes < 16 ? 16 : bytes)},
+                   like.options().dtype(at::kByte));
+}
+
+// ---------------------------------------------------------------------------
+at::Tensor gate_logits(const at::Tensor& h, const at::Tensor& wg,
+                       const c10::optional<at::Tensor>& bias) {
+  check_cuda(h, "h");
+  check_cuda(wg, "wg");
+  TORCH_CHECK(h.dim() == 2 && wg.dim() == 2 && h.size(1) == wg.size(1), "gate_logits: shapes");
+  TORCH_CHECK(h.scalar_type() == at::kHalf && wg.scalar_type() == at::kHalf,
+              "gate_logits: fp16 inputs expected");
+  const float* b = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    check_cuda(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == wg.size(0), "bias");
+    b = bias->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(h.device());
+  auto out = at::empty({h.size(0), wg.size(0)}, h.options().dtype(at::kFloat));
+  check_status(lr_gate_logits(h.data_ptr(), wg.data_ptr(), b, int(h.size(0)), int(h.size(1)),
+                              int(wg.size(0)), out.data_ptr<float>(), cur_stream()),
+               "gate_logits");
+  return out;
+}
+
+std::vector<at::Tensor> topk_gating_dispatch(const c10::optional<at::Tensor>& x,
+                                             const at::Tensor& logits, int64_t k,
+                                             int64_t capacity, double lbw, bool fill_dropped,
+                                             bool with_aux, const c10::optional<at::Tensor>& err) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.scalar_type() == at::kFloat, "logits: (T,E) fp32");
+  const int64_t T = logits.size(0), E = logits.size(1), S = T * k;
+  c10::cuda::CUDAGuard g(logits.device());
+  auto iopt = logits.options().dtype(at::kInt);
+  auto fopt = logits.options().dtype(at::kFloat);
+  auto ids = at::empty({S}, iopt);
+  auto gw = at::empty({S}, fopt);
+  auto tok = at::empty({S}, iopt);
+  auto offsets = at::empty({E + 1}, iopt);
+  auto kept = at::empty({E}, iopt);
+  auto aux = at::zeros({}, fopt);
+  auto rw = at::empty({S}, fopt);
+  auto src = at::empty({S}, iopt);
+  auto pos = at::empty({S}, iopt);
+  at::Tensor permuted;
+  int64_t d = 0;
+  if (x.has_value() && x->defined()) {
+    check_cuda(*x, "x");
+    TORCH_CHECK(x->dim() == 2 && x->size(0) == T && x->scalar_type() == at::kHalf,
+                "x: (T,d) fp16");
+    d = x->size(1);
+    permuted = fill_dropped ? at::empty({S, d}, x->options()) : at::empty({S, d}, x->options());
+  } else {
+    permuted = at::empty({0}, logits.options().dtype(at::kHalf));
+  }
+  auto ws = workspace(lr_route_workspace_bytes(int(T), int(k), int(E)), logits);
+  check_status(
+      lr_topk_gating_dispatch(permuted.numel() ? x->data_ptr() : nullptr, logits.data_ptr<float>(),
+                              int(T), int(d), int(E), int(k), int(capacity), float(lbw),
+                              fill_dropped ? 1 : 0, ids.data_ptr<int32_t>(), gw.data_ptr<float>(),
+                              tok.data_ptr<int32_t>(), offsets.data_ptr<int32_t>(),
+                              kept.data_ptr<int32_t>(), with_aux ? aux.data_ptr<float>() : nullptr,
+                              permuted.numel() ? permuted.data_ptr() : nullptr,
+                              rw.data_ptr<float>(), src.data_ptr<int32_t>(),
+                              pos.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.numel()),
+                              err_ptr(err), cur_stream()),
+      "topk_gating_dispatch");
+  return {ids, gw, tok, offsets, kept, aux, permuted, rw, src, pos};
+}
+
+std::vector<at::Tensor> expert_routing_forward(const at::Tensor& tokens,
+                                               const at::Tensor& expert_ids,
+                                               const at::Tensor& gate_weights,
+                                               const at::Tensor& token_indices,
+                                               int64_t num_experts, int64_t capacity,
+                                               bool fill_dropped,
+                                               const c10::optional<at::Tensor>& err) {
+  check_cuda(tokens, "tokens");
+  check_cuda(expert_ids, "expert_ids");
+  check_cuda(gate_weights, "gate_weights");
+  check_cuda(token_indices, "token_indices");
+  TORCH_CHECK(tokens.dim() == 2 && tokens.scalar_type() == at::kHalf, "tokens: (T,d) fp16");
+  TORCH_CHECK(expert_ids.scalar_type() == at::kInt && token_indices.scalar_type() == at::kInt,
+              "expert_ids / token_indices: int32");
+  TORCH_CHECK(gate_weights.scalar_type() == at::kFloat, "gate_weights: fp32");
+  const int64_t S = expert_ids.numel(), T = tokens.size(0), d = tokens.size(1);
+  TORCH_CHECK(gate_weights.numel() == S && token_indices.numel() == S, "slot counts differ");
+  c10::cuda::CUDAGuard g(tokens.device());
+  auto iopt = tokens.options().dtype(at::kInt);
+  auto permuted = at::empty({S, d}, tokens.options());
+  auto offsets = at::empty({num_experts + 1}, iopt);
+  auto rw = at::empty({S}, tokens.options().dtype(at::kFloat));
+  auto src = at::empty({S}, iopt);
+  auto kept = at::empty({num_experts}, iopt);
+  auto pos = at::empty({S}, iopt);
+  auto ws = workspace(lr_dispatch_workspace_bytes(int(S), int(num_experts)), tokens);
+  check_status(lr_expert_routing_forward(
+                   tokens.data_ptr(), expert_ids.data_ptr<int32_t>(), gate_weights.data_ptr<float>(),
+                   token_indices.data_ptr<int32_t>(), int(T), int(d), int(S), int(num_experts),
+                   int(capacity), fill_dropped ? 1 : 0, permuted.data_ptr(),
+                   offsets.data_ptr<int32_t>(), rw.data_ptr<float>(), src.data_ptr<int32_t>(),
+                   kept.data_ptr<int32_t>(), pos.data_ptr<int32_t>(), ws.data_ptr(),
+                   size_t(ws.numel()), err_ptr(err), cur_stream()),
+               "expert_routing_forward");
+  return {permuted, offsets, rw, src, kept, pos};
+}
+
+at::Tensor combine(const at::Tensor& y, const at::Tensor& gate_weights, const at::Tensor& slot_pos,
+                   int64_t num_tokens, int64_t k) {
+  check_cuda(y, "y");
+  check_cuda(gate_weights, "gate_weights");
+  check_cuda(slot_pos, "slot_pos");
+  TORCH_CHECK(y.dim() == 2 && y.scalar_type() == at::kHalf, "y: (R,d) fp16");
+  TORCH_CHECK(slot_pos.numel() == num_tokens * k && gate_weights.numel() == num_tokens * k,
+              "slot counts");
+  c10::cuda::CUDAGuard g(y.device());
+  auto out = at::empty({num_tokens, y.size(1)}, y.options());
+  check_status(lr_combine(y.data_ptr(), gate_weights.data_ptr<float>(), slot_pos.data_ptr<int32_t>(),
+                          int(num_tokens), int(k), int(y.size(1)), out.data_ptr(), cur_stream()),
+               "combine");
+  return out;
+}
+
+at::Tensor expert_routing_gather(const at::Tensor& y, const at::Tensor& routing_w,
+                                 const at::Tensor& source_idx, int64_t num_tokens,
+                                 const c10::optional<at::Tensor>& err) {
+  check_cuda(y, "expert_output");
+  check_cuda(routing_w, "routing_weights");
+  check_cuda(source_idx, "source_indices");
+  TORCH_CHECK(y.dim() == 2 && y.scalar_type() == at::kHalf, "expert_output: (R,d) fp16");
+  TORCH_CHECK(routing_w.scalar_type() == at::kFloat && source_idx.scalar_type() == at::kInt,
+              "routing_weights fp32 / source_indices int32");
+  const int64_t R = y.size(0);
+  TORCH_CHECK(routing_w.numel() == R && source_idx.numel() == R, "row counts differ");
+  c10::cuda::CUDAGuard g(y.device());
+  auto out = at::empty({num_tokens, y.size(1)}, y.options());
+  auto ws = workspace(lr_gather_workspace_bytes(int(R), int(num_tokens)), y);
+  check_status(lr_expert_routing_gather(y.data_ptr(), routing_w.data_ptr<float>(),
+                                        source_idx.data_ptr<int32_t>(), int(R), int(y.size(1)),
+                                        int(num_tokens), out.data_ptr(), ws.data_ptr(),
+                                        size_t(ws.numel()), err_ptr(err), cur_stream()),
+               "expert_routing_gather");
+  return out;
+}
+
+// Host-side encoding of the per-expert weight table; returns a CPU uint8 tensor.
+at::Tensor encode_weight_table(const std::vector<c10::optional<at::Tensor>>& qweights,
+                               const std::vector<c10::optional<at::Tensor>>& scales,
+                               const std::vector<c10::optional<at::Tensor>>& zeros,
+                               int64_t num_experts, int64_t d_model, int64_t d_ff,
+                               int64_t group_size, bool gated) {
+  TORCH_CHECK(int64_t(qweights.size()) == 3 * num_experts &&
+                  int64_t(scales.size()) == 3 * num_experts &&
+                  int64_t(zeros.size()) == 3 * num_experts,
+              "encode_weight_table: expected 3 entries per expert");
+  std::vector<lr_expert_weights> ex(num_experts);
+  std::memset(ex.data(), 0, sizeof(lr_expert_weights) * ex.size());
+  c10::optional<c10::Device> dev;
+  for (int64_t e = 0; e < num_experts; ++e) {
+    for (int m = 0; m < 3; ++m) {
+      const auto& q = qweights[e * 3 + m];
+      if (!q.has_value() || !q->defined()) continue;
+      const auto& s = scales[e * 3 + m];
+      const auto& z = zeros[e * 3 + m];
+      TORCH_CHECK(s.has_value() && z.has_value(), "scales/zeros missing for a present matrix");
+      check_cuda(*q, "qweight");
+      check_cuda(*s, "scales");
+      check_cuda(*z, "zeros");
+      TORCH_CHECK(q->scalar_type() == at::kInt && z->scalar_type() == at::kInt &&
+                      s->scalar_type() == at::kHalf,
+                  "qweight/zeros int32, scales fp16");
+      const int64_t K = (m < 2) ? d_model : d_ff, N = (m < 2) ? d_ff : d_model;
+      TORCH_CHECK(q->size(0) == K && q->size(1) == N / 8, "qweight shape");
+      TORCH_CHECK(s->size(0) == K / group_size && s->size(1) == N, "scales shape");
+      TORCH_CHECK(z->size(0) == K / group_size && z->size(1) == N / 8, "zeros shape");
+      if (!dev) dev = q->device();
+      ex[e].qweight[m] = q->data_ptr<int32_t>();
+      ex[e].scales[m] = s->data_ptr();
+      ex[e].zeros[m] = z->data_ptr<int32_t>();
+    }
+  }
+  TORCH_CHECK(dev.has_value(), "encode_weight_table: no matrices");
+  c10::cuda::CUDAGuard g(*dev);
+  const size_t bytes = lr_weight_table_bytes(int(num_experts));
+  // 128-byte aligned host staging
+  auto host = at::empty({int64_t(bytes + 128)}, at::TensorOptions().dtype(at::kByte));
+  const uintptr_t base = reinterpret_cast<uintptr_t>(host.data_ptr());
+  const int64_t off = int64_t((128 - (base & 127)) & 127);
+  auto view = host.narrow(0, off, int64_t(bytes));
+  check_status(lr_encode_weight_table(ex.data(), int(num_experts), int(d_model), int(d_ff),
+                                      int(group_size), gated ? 1 : 0, view.data_ptr(), bytes),
+               "encode_weight_table");
+  return view.clone();
+}
+
+at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int64_t mode,
+                              int64_t mat, const at::Tensor& A, int64_t N,
+                              const c10::optional<at::Tensor>& seg_start,
+                              const c10::optional<at::Tensor>& seg_len, int64_t max_rows,
+                              const c10::optional<at::Tensor>& out,
+                              const c10::optional<at::Tensor>& err) {
+  check_cuda(table, "table");
+  check_cuda(A, "A");
+  TORCH_CHECK(A.dim() == 2 && A.scalar_type() == at::kHalf, "A: (R,K) fp16");
+  c10::cuda::CUDAGuard g(A.device());
+  at::Tensor C;
+  if (out.has_value() && out->defined()) {
+    C = *out;
+    check_cuda(C, "out");
+    TORCH_CHECK(C.scalar_type() == at::kHalf && C.dim() == 2 && C.size(0) == A.size(0) &&
+                    C.size(1) == N,
+                "out: (R,N) fp16");
+  } else {
+    C = at::empty({A.size(0), N}, A.options());
+  }
+  const int32_t* ss = nullptr;
+  const int32_t* sl = nullptr;
+  if (seg_start.has_value() && seg_start->defined()) {
+    check_cuda(*seg_start, "seg_start");
+    check_cuda(*seg_len, "seg_len");
+    ss = seg_start->data_ptr<int32_t>();
+    sl = seg_len->data_ptr<int32_t>();
+  }
+  check_status(lr_grouped_w4a16_gemm(table.data_ptr(), int(num_experts), int(mode), int(mat),
+                                     A.data_ptr(), int(A.size(0)), int(A.size(1)), int(N), ss, sl,
+                                     int(max_rows), C.data_ptr(), nullptr, 0, err_ptr(err),
+                                     cur_stream()),
+               "grouped_w4a16_gemm");
+  return C;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(lightning_router, m) {
+  m.def("gate_logits(Tensor h, Tensor wg, Tensor? bias) -> Tensor");
+  m.def(
+      "topk_gating_dispatch(Tensor? x, Tensor logits, int k, int capacity, float lbw, "
+      "bool fill_dropped, bool with_aux, Tensor? err) -> Tensor[]");
+  m.def(
+      "expert_routing_forward(Tensor tokens, Tensor expert_ids, Tensor gate_weights, "
+      "Tensor token_indices, int num_experts, int capacity, bool fill_dropped, Tensor? err) -> "
+      "Tensor[]");
+  m.def("combine(Tensor y, Tensor gate_weights, Tensor slot_pos, int num_tokens, int k) -> Tensor");
+  m.def(
+      "expert_routing_gather(Tensor expert_output, Tensor routing_weights, Tensor "
+      "source_indices, int num_tokens, Tensor? err) -> Tensor");
+  m.def(
+      "encode_weight_table(Tensor?[] qweights, Tensor?[] scales, Tensor?[] zeros, int "
+      "num_experts, int d_model, int d_ff, int group_size, bool gated) -> Tensor");
+  m.def(
+      "grouped_w4a16_gemm(Tensor table, int num_experts, int mode, int mat, Tensor A, int N, "
+      "Tensor? seg_start, Tensor? seg_len, int max_rows, Tensor? out, Tensor? err) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
+  m.impl("gate_logits", &gate_logits);
+  m.impl("topk_gating_dispatch", &topk_gating_dispatch);
+  m.impl("expert_routing_forward", &expert_routing_forward);
+  m.impl("combine", &combine);
+  m.impl("expert_routing_gather", &expert_routing_gather);
+  m.impl("grouped_w4a16_gemm", &grouped_w4a16_gemm);
+}
+
+TORCH_LIBRARY_IMPL(lightning_router, CompositeExplicitAutograd, m) {
+  m.impl("encode_weight_table", &encode_weight_table);
+}

@@ -1,0 +1,76 @@
+"""CPU checks of the C ABI boundary: the library loads, exports every symbol the
+header declares, and its host-only entry points behave (no device calls)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from lightning_router import _ext
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "lightning_router.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(lr_[a-z0-9_]+)\s*\(", text))
+
+
+def test_header_and_loader_agree():
+    assert declared_symbols() == set(_ext.C_ABI_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _ext.clib()
+    for name in sorted(declared_symbols()):
+        assert hasattr(lib, name), name
+
+
+def test_status_strings_and_version():
+    lib = _ext.clib()
+    assert lib.lr_abi_version() == 1
+    assert lib.lr_status_string(0) == b"ok"
+    assert b"invalid" in lib.lr_status_string(-1)
+    assert b"workspace" in lib.lr_status_string(-4)
+
+
+def test_workspace_queries_are_host_only():
+    lib = _ext.clib()
+    assert lib.lr_route_workspace_bytes(16384, 2, 8) >= 256 + 2 * 64 * 8 * 4
+    assert lib.lr_dispatch_workspace_bytes(1 << 20, 64) > 0
+    assert lib.lr_gather_workspace_bytes(1000, 500) >= 4 * (1000 * 2 + 500 * 3)
+    assert lib.lr_weight_table_bytes(8) == 8 * lib.lr_weight_table_bytes(1)
+    assert lib.lr_weight_table_bytes(1) % 128 == 0
+
+
+def test_argument_validation_without_device():
+    """Invalid shapes are rejected before any CUDA call."""
+    lib = _ext.clib()
+    # d not a multiple of 16
+    assert lib.lr_gate_logits(None, None, None, 4, 10, 8, None, None) == -1
+    # E > 64 for the gating kernel
+    assert lib.lr_topk_gating_dispatch(None, None, 4, 64, 65, 2, 8, ctypes.c_float(0.01), 0,
+                                       None, None, None, None, None, None, None, None, None,
+                                       None, None, ctypes.c_size_t(0), None, None) == -1
+    # K not a multiple of 64
+    assert lib.lr_grouped_w4a16_gemm(ctypes.c_void_p(128), 1, 0, 2, None, 4, 100, 64, None, None,
+                                     4, None, None, ctypes.c_size_t(0), None, None) in (-1, -2)
+
+
+def test_torch_ops_register():
+    ops = _ext.ops()
+    for name in ("gate_logits", "topk_gating_dispatch", "expert_routing_forward", "combine",
+                 "expert_routing_gather", "encode_weight_table", "grouped_w4a16_gemm"):
+        assert hasattr(ops, name), name
+
+
+def test_cpu_tensors_fail_loudly():
+    import torch
+    from lightning_router.models.gating import TopKGating
+    gate = TopKGating(64, 4, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gate(torch.randn(3, 64))

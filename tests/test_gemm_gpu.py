@@ -1,0 +1,160 @@
+"""GPU numerics of the tcgen05 W4A16 GEMM against a plain fp32 reference of the
+same op: ``A.float() @ dequantize(B).float()`` (the dequantized weights are
+bit-exact fp16, so the only differences are accumulation order and the final
+fp16 rounding).  Tolerance: relative L2 <= 1e-3 and max-abs <= 2e-2 * max|ref|.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _quant(K, N, g, seed, scale=0.02):
+    from lightning_router.quantization.pack_weights import dequantize_tensor, quantize_tensor
+    gen = torch.Generator().manual_seed(seed)
+    W = (torch.randn(K, N, generator=gen) * scale).half()
+    qw, s, z = quantize_tensor(W, g)
+    return qw.to(DEV), s.to(DEV), z.to(DEV), dequantize_tensor(qw, s, z, g, N).to(DEV)
+
+
+def _check(out, ref, rel=1e-3, absf=2e-2):
+    out, ref = out.float(), ref.float()
+    err = (out - ref).norm() / ref.norm().clamp_min(1e-30)
+    mx = (out - ref).abs().max()
+    assert torch.isfinite(out).all()
+    assert err <= rel, f"rel-L2 {err:.3e}"
+    assert mx <= absf * ref.abs().max().clamp_min(1e-30), f"max-abs {mx:.3e}"
+
+
+def test_reference_output_shape_and_error():
+    """Mirrors the reference's tests/test_quantization.py:61-93."""
+    from lightning_router.kernels.quantized_matmul import quantized_matmul
+    M, K, N = 32, 256, 64
+    qw, s, z, Wd = _quant(K, N, 128, 0)
+    A = torch.randn(M, K, device=DEV).half()
+    C = quantized_matmul(A, qw, s, z, N=N, group_size=128)
+    assert C.shape == (M, N)
+    ref = A @ Wd
+    rel_err = (C - ref).float().norm() / ref.float().norm()
+    assert rel_err < 0.2
+    _check(C, A.float() @ Wd.float())
+
+
+@pytest.mark.parametrize("M,K,N,g", [
+    (1, 64, 64, 64), (7, 256, 128, 128), (16, 1024, 256, 64), (33, 512, 96, 128),
+    (100, 1024, 384, 128), (128, 256, 128, 64), (255, 1024, 4096, 128), (256, 2048, 1408, 64),
+    (300, 4096, 512, 128), (1000, 1024, 1024, 128), (4096, 1024, 256, 128),
+])
+def test_quantized_matmul_shapes(M, K, N, g):
+    from lightning_router.kernels.quantized_matmul import quantized_matmul
+    qw, s, z, Wd = _quant(K, N, g, M + K + N)
+    A = torch.randn(M, K, device=DEV).half()
+    C = quantized_matmul(A, qw, s, z, N=N, group_size=g)
+    _check(C, A.float() @ Wd.float())
+
+
+@pytest.mark.parametrize("name", ["m1", "m2"])
+def test_matches_reference_triton_fixture(name):
+    from lightning_router.kernels.quantized_matmul import quantized_matmul
+    zz = golden("qmm_interp")
+    A = torch.from_numpy(zz[f"{name}_a"]).to(DEV)
+    C = quantized_matmul(A, torch.from_numpy(zz[f"{name}_qweight"]).to(DEV),
+                         torch.from_numpy(zz[f"{name}_scales"]).to(DEV),
+                         torch.from_numpy(zz[f"{name}_zeros"]).to(DEV),
+                         N=int(zz[f"{name}_N"]), group_size=int(zz[f"{name}_gs"]))
+    ref = zz[f"{name}_c"].astype(np.float32)
+    c = C.float().cpu().numpy()
+    assert np.linalg.norm(c - ref) / np.linalg.norm(ref) < 2e-3
+
+
+def _grouped_case(E, d, f, g, lens, mode, seed):
+    """Build E experts and row segments; returns (table, A, seg_start, seg_len, refs)."""
+    from lightning_router.kernels.quantized_matmul import weight_table
+    gen = torch.Generator().manual_seed(seed)
+    starts, pos = [], 0
+    for L in lens:
+        starts.append(pos)
+        pos += L + int(torch.randint(0, 5, (1,), generator=gen))  # gaps between segments
+    R = pos + 3
+    A = torch.randn(R, d, generator=gen).half().to(DEV)
+    q, s, z, deq = [], [], [], []
+    for e in range(E):
+        de = {}
+        for m, (K, N) in enumerate([(d, f), (d, f), (f, d)]):
+            qw, sc, zr, Wd = _quant(K, N, g, seed * 100 + e * 3 + m)
+            q.append(qw), s.append(sc), z.append(zr)
+            de[m] = Wd
+        deq.append(de)
+    table = weight_table(q, s, z, E, d, f, g, True)
+    ss = torch.tensor(starts, dtype=torch.int32, device=DEV)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    return table, A, ss, sl, deq, R
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("lens,maxr", [([0, 1, 100, 300], 300), ([16, 16, 3, 0], 16),
+                                       ([20, 7, 31, 12], 32), ([600, 260, 5, 129], 600)])
+def test_grouped_modes(mode, lens, maxr):
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E, d, f, g = 4, 256, 384, 64
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, mode, seed=len(lens) + maxr + mode)
+    N = f
+    sentinel = torch.full((R, N), 7.0, dtype=torch.float16, device=DEV)
+    out = grouped_w4a16(table, E, mode, 1, A, N, ss, sl, maxr, out=sentinel.clone())
+    covered = torch.zeros(R, dtype=torch.bool, device=DEV)
+    for e, L in enumerate(lens):
+        st = int(ss[e])
+        if L == 0:
+            continue
+        x = A[st:st + L].float()
+        if mode == 0:
+            ref = x @ deq[e][1].float()
+        elif mode == 1:
+            ref = torch.nn.functional.silu(x @ deq[e][1].float())
+        else:
+            ref = torch.nn.functional.silu(x @ deq[e][0].float()) * (x @ deq[e][1].float())
+        _check(out[st:st + L], ref)
+        covered[st:st + L] = True
+    # rows outside the segments are not written
+    assert torch.equal(out[~covered], sentinel[~covered])
+
+
+def test_grouped_down_projection_long_k():
+    """K = d_ff = 14336 (the Mixtral down projection), a few rows per expert."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16, weight_table
+    E, d, f, g = 2, 256, 14336, 128
+    q, s, z, deq = [], [], [], []
+    for e in range(E):
+        for m, (K, N) in enumerate([(d, f), (d, f), (f, d)]):
+            if m < 2:
+                q.append(None), s.append(None), z.append(None)
+                continue
+            qw, sc, zr, Wd = _quant(K, N, g, 900 + e)
+            q.append(qw), s.append(sc), z.append(zr)
+            deq.append(Wd)
+    table = weight_table(q, s, z, E, d, f, g, False)
+    A = torch.randn(40, f, device=DEV).half()
+    ss = torch.tensor([0, 20], dtype=torch.int32, device=DEV)
+    sl = torch.tensor([20, 17], dtype=torch.int32, device=DEV)
+    out = grouped_w4a16(table, E, 0, 2, A, d, ss, sl, 20)
+    _check(out[0:20], A[0:20].float() @ deq[0].float())
+    _check(out[20:37], A[20:37].float() @ deq[1].float())
+
+
+def test_segment_overflow_is_flagged_and_clamped():
+    from lightning_router import _ext
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E, d, f, g = 2, 128, 128, 64
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, [10, 10], 0, seed=1)
+    _ext.check_device_errors()
+    bad = torch.tensor([0, R - 2], dtype=torch.int32, device=DEV)   # second segment runs past R
+    grouped_w4a16(table, E, 0, 1, A, f, bad, sl, 10)
+    with pytest.raises(RuntimeError, match="segment"):
+        _ext.check_device_errors()
