@@ -218,17 +218,22 @@ LR_DEVICE void umma_commit(uint64_t* bar) {
       : "memory");
 }
 
-// 32 lanes x 32 bit, 16 consecutive columns per thread.
-LR_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+// 32 lanes x 32 bit, 16 consecutive columns per thread.  The load and its
+// wait are one asm statement: tcgen05.ld writes its destination registers
+// asynchronously, so no instruction may read them before tcgen05.wait::ld,
+// and a separate wait statement would not stop the compiler from scheduling
+// uses of the outputs ahead of it.
+LR_DEVICE void tmem_ld_32x32b_x16_sync(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+      : "r"(taddr)
+      : "memory");
 }
-LR_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 format, version 1).
 //   start address, leading byte offset and stride byte offset are in 16-byte units;

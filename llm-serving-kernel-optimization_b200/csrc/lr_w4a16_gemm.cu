@@ -341,7 +341,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      if (!ok) {
+      if (ok) {
+        // Producer tail: wait until the MMA has released every stage.  The
+        // releases are tcgen05.commit arrivals that complete asynchronously;
+        // leaving before they land would let them hit the barriers of the next
+        // CTA placed on this SM.
+        for (int i = 0; i < STAGES; ++i, ++it) {
+          if (!wait_any(&empty[it % STAGES], ((it / STAGES) & 1) ^ 1, s_abort, err)) break;
+        }
+      } else {
         // let in-flight copies land before the CTA exits
         const int first = it - STAGES < 0 ? 0 : it - STAGES;
         for (int i = first; i < it; ++i) wait_drain(&full[i % STAGES], (i / STAGES) & 1);
@@ -432,6 +440,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&dfull[q]);
       }
     }
+    // Dequant tail: the last operand buffers are released by asynchronous
+    // tcgen05.commit arrivals; wait for them before the CTA can exit.
+    for (int i = 0; ok && i < kDStages; ++i, ++it) {
+      if (!wait_any(&dempty[it % kDStages], ((it / kDStages) & 1) ^ 1, s_abort, err)) break;
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int etid = threadIdx.x;  // 0..127 == TMEM lane == feature in tile
@@ -458,8 +471,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < BN / 16; ++c) {
         if (c * 16 >= rows_valid) break;
         uint32_t v[16];
-        tmem_ld_32x32b_x16(tbase + c * 16, v);
-        tmem_ld_wait();
+        tmem_ld_32x32b_x16_sync(tbase + c * 16, v);
         const int nrow = min(16, rows_valid - c * 16);
         if (MODE != LR_FFN_MODE_SWIGLU) {
           __half* stage = reinterpret_cast<__half*>(sC);  // [16][128]

@@ -7,9 +7,10 @@ and ``MoELayer`` (:func:`grouped_w4a16`).
 Weights stay in the reference's packed format (``qweight`` (K, N/8) int32,
 ``scales`` (K/g, N) fp16, ``zeros`` (K/g, N/8) int32).  A small per-expert
 "weight table" (TMA descriptors + pointers, ~900 B per expert) is encoded once
-per weight set and cached on the device, keyed by the buffers' addresses and
-shapes (the table holds only addresses and strides, so it stays valid when a
-buffer is updated in place).  Limits of the tcgen05 kernel: ``K % 64 == 0``,
+per weight set and kept on the device together with references to the weight
+tensors it points to (it holds only addresses and strides, so it stays valid
+when a buffer is updated in place).  Modules keep their own tables; the
+functional :func:`quantized_matmul` uses a small bounded cache.  Limits of the tcgen05 kernel: ``K % 64 == 0``,
 ``group_size % 64 == 0``, ``N % 32 == 0`` (``N % 64 == 0`` for the fused SwiGLU
 mode), at most 256 experts per launch.
 """
@@ -17,6 +18,7 @@ mode), at most 256 experts per launch.
 from __future__ import annotations
 
 from collections import OrderedDict
+from typing import NamedTuple
 
 import torch
 
@@ -26,8 +28,18 @@ FFN_MODE_PLAIN = _ext.FFN_MODE_PLAIN
 FFN_MODE_SILU = _ext.FFN_MODE_SILU
 FFN_MODE_SWIGLU = _ext.FFN_MODE_SWIGLU
 
-_TABLE_CACHE: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
-_TABLE_CACHE_MAX = 64
+class WeightTable(NamedTuple):
+    """Device table plus the weight tensors it points to.
+
+    The table holds raw addresses; keeping ``refs`` alive keeps those addresses
+    valid for as long as the table is in use.
+    """
+    table: torch.Tensor
+    refs: tuple
+
+
+_TABLE_CACHE: "OrderedDict[tuple, WeightTable]" = OrderedDict()
+_TABLE_CACHE_MAX = 16
 
 
 def _key(t: torch.Tensor | None):
@@ -37,15 +49,15 @@ def _key(t: torch.Tensor | None):
 
 
 def weight_table(qweights, scales, zeros, num_experts: int, d_model: int, d_ff: int,
-                 group_size: int, gated: bool) -> torch.Tensor:
+                 group_size: int, gated: bool, cache: bool = True) -> WeightTable:
     """Device-resident weight table for ``num_experts`` experts.
 
     ``qweights[e*3 + m]`` (m = 0 gate, 1 up, 2 down; ``None`` when absent) with
     gate/up of shape (d_model, d_ff/8) and down of shape (d_ff, d_model/8).
+    Cached entries keep their weight tensors alive (at most 16 entries).
     """
-    key = (tuple(_key(t) for t in qweights), tuple(_key(t) for t in scales),
-           tuple(_key(t) for t in zeros), num_experts, d_model, d_ff, group_size, gated)
-    hit = _TABLE_CACHE.get(key)
+    key = table_key(qweights, scales, zeros, num_experts, d_model, d_ff, group_size, gated)
+    hit = _TABLE_CACHE.get(key) if cache else None
     if hit is not None:
         _TABLE_CACHE.move_to_end(key)
         return hit
@@ -59,19 +71,31 @@ def weight_table(qweights, scales, zeros, num_experts: int, d_model: int, d_ff: 
     table = torch.empty(host.numel(), dtype=torch.uint8, device=dev)
     assert table.data_ptr() % 128 == 0
     table.copy_(host)
-    _TABLE_CACHE[key] = table
-    while len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
-        _TABLE_CACHE.popitem(last=False)
-    return table
+    refs = tuple(t for t in (*qweights, *scales, *zeros) if t is not None)
+    wt = WeightTable(table, refs)
+    if cache:
+        _TABLE_CACHE[key] = wt
+        while len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
+            _TABLE_CACHE.popitem(last=False)
+    return wt
 
 
-def grouped_w4a16(table: torch.Tensor, num_experts: int, mode: int, mat: int, A: torch.Tensor,
+def table_key(qweights, scales, zeros, *extra) -> tuple:
+    return (tuple(_key(t) for t in qweights), tuple(_key(t) for t in scales),
+            tuple(_key(t) for t in zeros), *extra)
+
+
+def clear_weight_tables() -> None:
+    _TABLE_CACHE.clear()
+
+
+def grouped_w4a16(table: WeightTable, num_experts: int, mode: int, mat: int, A: torch.Tensor,
                   N: int, seg_start: torch.Tensor | None, seg_len: torch.Tensor | None,
                   max_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Grouped GEMM over expert row segments; see ``lr_grouped_w4a16_gemm``."""
     _ext.require_cuda(A)
     err = _ext.error_word(A.device.index)
-    return _ext.ops().grouped_w4a16_gemm(table, int(num_experts), int(mode), int(mat),
+    return _ext.ops().grouped_w4a16_gemm(table.table, int(num_experts), int(mode), int(mat),
                                          A.contiguous(), int(N), seg_start, seg_len,
                                          int(max_rows), out, err)
 
@@ -102,6 +126,9 @@ def quantized_matmul(
         raise NotImplementedError(f"W4A16 kernel needs K % 64 == 0 and N % 32 == 0 (K={K}, N={N})")
     if M == 0:
         return torch.empty(0, N, dtype=torch.float16, device=A.device)
+    # cache only tables over the caller's own tensors, never over temporaries
+    persistent = B_packed.is_contiguous() and scales.is_contiguous() and zeros.is_contiguous()
     table = weight_table([None, None, B_packed.contiguous()], [None, None, scales.contiguous()],
-                         [None, None, zeros.contiguous()], 1, N, K, group_size, False)
+                         [None, None, zeros.contiguous()], 1, N, K, group_size, False,
+                         cache=persistent)
     return grouped_w4a16(table, 1, FFN_MODE_PLAIN, 2, A, N, None, None, M)

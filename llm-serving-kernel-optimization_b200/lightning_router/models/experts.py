@@ -19,7 +19,18 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from lightning_router.kernels.quantized_matmul import (
-    FFN_MODE_PLAIN, FFN_MODE_SILU, FFN_MODE_SWIGLU, grouped_w4a16, weight_table)
+    FFN_MODE_PLAIN, FFN_MODE_SILU, FFN_MODE_SWIGLU, WeightTable, grouped_w4a16, table_key,
+    weight_table)
+
+
+def _module_table(cache: dict, q, s, z, n, d, f, g, gated) -> WeightTable:
+    """Per-module table cache keyed by the buffers' addresses and shapes."""
+    key = table_key(q, s, z, n, d, f, g, gated)
+    wt = cache.get(key)
+    if wt is None:
+        cache.clear()
+        wt = cache[key] = weight_table(q, s, z, n, d, f, g, gated, cache=False)
+    return wt
 
 _MATS = ("gate", "up", "down")
 
@@ -37,6 +48,7 @@ class ExpertFFN(nn.Module):
         self.quantized = quantized
         self.group_size = group_size
         self.activation = activation
+        self._tables: dict = {}
         gated = activation == "swiglu"
         if not quantized:
             if gated:
@@ -79,8 +91,8 @@ class ExpertFFN(nn.Module):
                 return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
             return self.down_proj(F.silu(self.up_proj(x)))
         q, s, z = self.quant_tensors()
-        table = weight_table(q, s, z, 1, self.hidden_size, self.intermediate_size,
-                             self.group_size, self.gated)
+        table = _module_table(self._tables, q, s, z, 1, self.hidden_size,
+                              self.intermediate_size, self.group_size, self.gated)
         x = x.half().contiguous()
         M = x.shape[0]
         if M == 0:
@@ -106,12 +118,13 @@ class ExpertGroup(nn.Module):
         self.quantized = quantized
         self.group_size = group_size
         self.activation = activation
+        self._tables: dict = {}
         self.experts = nn.ModuleList([
             ExpertFFN(hidden_size, intermediate_size, quantized, group_size, activation)
             for _ in range(num_experts)
         ])
 
-    def table(self, first: int = 0, count: int | None = None) -> torch.Tensor:
+    def table(self, first: int = 0, count: int | None = None) -> WeightTable:
         count = self.num_experts - first if count is None else count
         q, s, z = [], [], []
         for e in range(first, first + count):
@@ -119,8 +132,13 @@ class ExpertGroup(nn.Module):
             q += qe
             s += se
             z += ze
-        return weight_table(q, s, z, count, self.hidden_size, self.intermediate_size,
-                            self.group_size, self.activation == "swiglu")
+        key = table_key(q, s, z)
+        hit = self._tables.get((first, count))
+        if hit is None or hit[0] != key:  # first use, or the buffers moved / were replaced
+            wt = weight_table(q, s, z, count, self.hidden_size, self.intermediate_size,
+                              self.group_size, self.activation == "swiglu", cache=False)
+            hit = self._tables[(first, count)] = (key, wt)
+        return hit[1]
 
     def forward_segments(self, x: torch.Tensor, seg_start: torch.Tensor, seg_len: torch.Tensor,
                          max_rows: int, first_expert: int = 0,

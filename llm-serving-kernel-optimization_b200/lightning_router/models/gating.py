@@ -35,8 +35,9 @@ class TopKGating(nn.Module):
             self.logit_bias = None
 
     def logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
-        h = hidden_states.reshape(-1, hidden_states.shape[-1])
-        return gate_logits(h, self.gate_proj.weight, self.logit_bias)
+        h = hidden_states.reshape(-1, hidden_states.shape[-1]).detach()
+        # inference path: the kernels have no backward, so no autograd graph is built
+        return gate_logits(h, self.gate_proj.weight.detach(), self.logit_bias)
 
     def forward(self, hidden_states: torch.Tensor):
         """Returns ``(expert_ids (S,) int32, gate_weights (S,) fp32,
