@@ -32,6 +32,7 @@ typedef struct CUstream_st* lr_stream_t; /* == cudaStream_t */
 #define LR_ERR_CUDA (-3)
 #define LR_ERR_WORKSPACE (-4)
 #define LR_ERR_NO_DEVICE (-5)
+#define LR_ERR_TOO_LARGE (-6) /* exceeds the fixed scratch of the allocation-free entry point */
 
 /* bits OR-ed into the device `err` word */
 #define LR_DEVERR_BAD_EXPERT 0x1     /* an expert id outside [0, E) */
@@ -75,6 +76,30 @@ int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, in
                             void* permuted, float* routing_w, int32_t* source_idx,
                             int32_t* slot_pos, void* workspace, size_t workspace_bytes,
                             int32_t* err, lr_stream_t stream);
+
+/* Allocation-free variant of lr_topk_gating_dispatch (no counterpart in the
+ * reference).  Same arguments and results, minus the workspace.  It is for
+ * callers that cannot allocate device memory: a serving host that owns all of
+ * it and passes this library pre-sized input and output buffers but no
+ * allocator, or a latency-critical loop where cudaMalloc, which synchronises
+ * the device, is not allowed.  Its scratch is a 1 MiB file-scope device array
+ * inside this library, held by every GPU that loads the library until the
+ * process exits, so 256 + 16 * ceil(T/256) * E bytes (each part rounded up to
+ * 256) must fit in 1 MiB: about 2 M tokens at E = 8, about 260 K tokens at
+ * E = 64.  Larger sizes return LR_ERR_TOO_LARGE before any work is queued.
+ * The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture begins.  Every call uses the same array and clears the
+ * part that must start at zero, so calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller.
+ * It allocates and frees nothing.                                          */
+int lr_topk_gating_dispatch_noalloc(const void* x, const float* logits, int T, int d, int E,
+                                    int k, int capacity, float load_balance_weight,
+                                    int fill_dropped, int32_t* expert_ids, float* gate_weights,
+                                    int32_t* token_indices, int32_t* offsets,
+                                    int32_t* kept_counts, float* aux_loss, void* permuted,
+                                    float* routing_w, int32_t* source_idx, int32_t* slot_pos,
+                                    int32_t* err, lr_stream_t stream);
 
 size_t lr_dispatch_workspace_bytes(int num_slots, int num_experts);
 

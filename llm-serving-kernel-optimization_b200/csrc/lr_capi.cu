@@ -30,6 +30,8 @@ extern "C" const char* lr_status_string(int status) {
       return "workspace missing or too small";
     case LR_ERR_NO_DEVICE:
       return "no sm_100 device";
+    case LR_ERR_TOO_LARGE:
+      return "size exceeds the 1 MiB static scratch of the allocation-free entry point";
     default:
       return "unknown status";
   }

@@ -872,3 +872,63 @@ extern "C" int lr_expert_routing_gather(const void* y, const float* routing_w,
   LR_LAUNCH_CHECK();
   return LR_OK;
 }
+
+// ===========================================================================
+// Allocation-free gating + dispatch
+// ===========================================================================
+// Some callers cannot allocate device memory: a serving host that owns every
+// byte of device memory and hands this library pre-sized input and output
+// buffers but no allocator, or a latency-critical loop that may not call
+// cudaMalloc (it synchronises the whole device).  For them the route scratch
+// lives in this file-scope device array instead of a caller workspace.  Every
+// GPU that loads the library holds it until the process exits.
+#include <mutex>
+
+static constexpr size_t kStaticRouteScratchBytes = size_t(1) << 20;  // 1 MiB
+static __device__ __align__(256) unsigned char g_route_scratch[kStaticRouteScratchBytes];
+
+static std::mutex g_route_scratch_mu;
+static void* g_route_scratch_dev[64];  // device address per device ordinal, found once
+
+// Device address of g_route_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress the first time each device calls, with that device current.
+static int route_scratch_address(void** out) {
+  int dev = 0;
+  LR_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_route_scratch_mu);
+  if (dev < 64 && g_route_scratch_dev[dev]) {
+    *out = g_route_scratch_dev[dev];
+    return LR_OK;
+  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
+  if (e != cudaSuccess || p == nullptr) return record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+  if (dev < 64) g_route_scratch_dev[dev] = p;
+  *out = p;
+  return LR_OK;
+}
+
+extern "C" int lr_topk_gating_dispatch_noalloc(const void* x, const float* logits, int T, int d,
+                                               int E, int k, int capacity,
+                                               float load_balance_weight, int fill_dropped,
+                                               int32_t* expert_ids, float* gate_weights,
+                                               int32_t* token_indices, int32_t* offsets,
+                                               int32_t* kept_counts, float* aux_loss,
+                                               void* permuted, float* routing_w,
+                                               int32_t* source_idx, int32_t* slot_pos,
+                                               int32_t* err, lr_stream_t stream) {
+  if (T <= 0 || E < 1 || E > 64 || k < 1 || k > kMaxTopK || k > E || capacity < 1)
+    return LR_ERR_INVALID_ARGUMENT;
+  const int B = (T + kRouteThreads - 1) / kRouteThreads;
+  if (route_ws_bytes_for(B, E, true) > kStaticRouteScratchBytes) return LR_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  const int rc = route_scratch_address(&scratch);
+  if (rc != LR_OK) return rc;
+  // The shared ticket word is cleared on the stream by the dispatch itself;
+  // the per-block counts, bases and sums are fully rewritten by every call.
+  return lr_topk_gating_dispatch(x, logits, T, d, E, k, capacity, load_balance_weight,
+                                 fill_dropped, expert_ids, gate_weights, token_indices, offsets,
+                                 kept_counts, aux_loss, permuted, routing_w, source_idx, slot_pos,
+                                 scratch, kStaticRouteScratchBytes, err, stream);
+}
