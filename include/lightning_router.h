@@ -77,6 +77,30 @@ int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, in
                             int32_t* slot_pos, void* workspace, size_t workspace_bytes,
                             int32_t* err, lr_stream_t stream);
 
+/* The two phases of lr_topk_gating_dispatch, for expert-parallel callers that
+ * exchange per-expert counts between them.
+ * lr_topk_route: gating, slot ranks inside their 256-token route blocks (left in
+ * slot_pos), local uncapped CSR `offsets`, kept_counts = min(count, capacity),
+ * the local aux loss and, if prob_sums != NULL, the per-expert sums of softmax
+ * probabilities over the T tokens (fp64).  The workspace carries the per-block
+ * bases to lr_permute_tokens and must not be reused in between.
+ * lr_permute_tokens: a slot whose rank inside this shard's expert segment is r
+ * is kept iff rank_base[e] + r < capacity (rank_base NULL => 0; rank_base[e] =
+ * slots of expert e in lower shards, so capacity follows the global slot
+ * order) and goes to row row_offsets[e] + r.  With compact != 0 dropped slots
+ * get no row (row_offsets then spans kept rows only) and slot_pos = -1.      */
+int lr_topk_route(const float* logits, int T, int E, int k, int capacity,
+                  float load_balance_weight, int32_t* expert_ids, float* gate_weights,
+                  int32_t* token_indices, int32_t* offsets, int32_t* kept_counts,
+                  float* aux_loss, double* prob_sums, int32_t* slot_pos, void* workspace,
+                  size_t workspace_bytes, int32_t* err, lr_stream_t stream);
+int lr_permute_tokens(const void* x, int T, int d, int E, int k, int capacity,
+                      const int32_t* expert_ids, const float* gate_weights,
+                      const int32_t* row_offsets, const int32_t* rank_base, int compact,
+                      int fill_dropped, int32_t* slot_pos, void* permuted, float* routing_w,
+                      int32_t* source_idx, const void* workspace, size_t workspace_bytes,
+                      lr_stream_t stream);
+
 /* Allocation-free variant of lr_topk_gating_dispatch (no counterpart in the
  * reference).  Same arguments and results, minus the workspace.  It is for
  * callers that cannot allocate device memory: a serving host that owns all of

@@ -129,7 +129,7 @@ LR_DEVICE void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
 }
 
-// 2D tiled load global -> shared, completion on an mbarrier (no multicast).
+// 2D tiled load global -> shared of this CTA, completion on an mbarrier.
 LR_DEVICE void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar, int32_t c0,
                            int32_t c1) {
   asm volatile(

@@ -171,7 +171,7 @@ LR_DEVICE int rank_chunk(int e, bool valid, int E, int32_t* s_wcnt, int32_t* s_r
 // writes offsets / kept_counts and the aux loss, resets the ticket.
 LR_DEVICE void route_tail(const RouteWs& ws, int B, int E, int C, int num_slots, int T, int k,
                           float lbw, int32_t* offsets, int32_t* kept_counts, float* aux_loss,
-                          int32_t* s_tot, double* s_P) {
+                          double* prob_sums, int32_t* s_tot, double* s_P) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int e = warp; e < E; e += kWarps) {
     int carry = 0;
@@ -205,6 +205,7 @@ LR_DEVICE void route_tail(const RouteWs& ws, int B, int E, int C, int num_slots,
       run += s_tot[e];
       offsets[e + 1] = run;
       if (kept_counts) kept_counts[e] = min(s_tot[e], C);
+      if (prob_sums) prob_sums[e] = s_P[e];
       aux += (double(s_tot[e]) / double(num_slots)) * (s_P[e] / double(T));
     }
     if (aux_loss) aux_loss[0] = static_cast<float>(double(lbw) * double(E) * aux);
@@ -234,7 +235,8 @@ __global__ void __launch_bounds__(kRouteThreads)
                       int32_t* __restrict__ expert_ids, float* __restrict__ gate_w,
                       int32_t* __restrict__ token_idx, int32_t* __restrict__ slot_rank,
                       int32_t* __restrict__ offsets, int32_t* __restrict__ kept_counts,
-                      float* __restrict__ aux_loss, RouteWs ws, int num_blocks) {
+                      float* __restrict__ aux_loss, double* __restrict__ prob_sums, RouteWs ws,
+                      int num_blocks) {
   __shared__ int32_t s_ids[kRouteThreads * kMaxTopK];
   __shared__ int32_t s_wcnt[kWarps * MAXE];
   __shared__ int32_t s_run[MAXE];
@@ -315,7 +317,8 @@ __global__ void __launch_bounds__(kRouteThreads)
     for (int i = 0; i < MAXE; ++i) p[i] = 0.f;
   }
   // per-warp probability sums (aux loss)
-  if (aux_loss) {
+  const bool want_p = aux_loss != nullptr || prob_sums != nullptr;
+  if (want_p) {
 #pragma unroll
     for (int i = 0; i < MAXE; ++i) {
       if (i < E) {
@@ -339,7 +342,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   }
   for (int i = tid; i < E; i += kRouteThreads) {
     ws.blk_counts[size_t(blockIdx.x) * E + i] = s_run[i];
-    if (aux_loss) {
+    if (want_p) {
       double sum = 0.0;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += double(s_pw[w * E + i]);
@@ -347,7 +350,8 @@ __global__ void __launch_bounds__(kRouteThreads)
     }
   }
   if (!arrive_last(ws.ticket, num_blocks, &s_last)) return;
-  route_tail(ws, num_blocks, E, C, T * k, T, k, lbw, offsets, kept_counts, aux_loss, s_tot, s_P);
+  route_tail(ws, num_blocks, E, C, T * k, T, k, lbw, offsets, kept_counts, aux_loss, prob_sums,
+             s_tot, s_P);
 }
 
 // ---------------------------------------------------------------------------
@@ -385,7 +389,8 @@ __global__ void __launch_bounds__(kRouteThreads)
   }
   for (int i = tid; i < E; i += kRouteThreads) ws.blk_counts[size_t(blockIdx.x) * E + i] = s_run[i];
   if (!arrive_last(ws.ticket, num_blocks, &s_last)) return;
-  route_tail(ws, num_blocks, E, C, S, 1, 1, 0.f, offsets, kept_counts, nullptr, s_tot, s_P);
+  route_tail(ws, num_blocks, E, C, S, 1, 1, 0.f, offsets, kept_counts, nullptr, nullptr, s_tot,
+             s_P);
 }
 
 // ---------------------------------------------------------------------------
@@ -402,27 +407,34 @@ LR_DEVICE uint4 ld_stream(const uint4* p) {
 constexpr int kCopyUnroll = 8;
 
 // gated routing: one warp per token, the row is read once and written k times.
+// A slot's rank inside this shard's expert segment is blk_base + block rank;
+// its expert-wide rank adds rank_base[e] (the slots of lower shards, or 0).
+// It is kept iff the expert-wide rank < C and lands at row_offsets[e] + rank.
+// With `compact`, dropped slots get no row (row_offsets then counts kept rows only).
 __global__ void __launch_bounds__(256)
     permute_tokens_kernel(const uint4* __restrict__ x, int T, int d8, int k, int E, int C,
                           int fill, const int32_t* __restrict__ expert_ids,
                           const float* __restrict__ gate_w, const int32_t* __restrict__ offsets,
+                          const int32_t* __restrict__ rank_base, int compact,
                           const int32_t* __restrict__ blk_base, int slots_per_blk,
                           int32_t* __restrict__ slot_pos, uint4* __restrict__ permuted,
                           float* __restrict__ routing_w, int32_t* __restrict__ src_idx) {
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
-  int my_dst = 0, my_kept = 0;
+  int my_dst = -1, my_kept = 0;
   if (lane < k) {
     const size_t s = size_t(t) * k + lane;
     const int e = expert_ids[s];
     const int r = slot_pos[s];
     const int rank = __ldg(blk_base + size_t(s / slots_per_blk) * E + e) + r;
-    my_dst = __ldg(offsets + e) + rank;
-    my_kept = rank < C;
+    my_kept = (rank_base ? __ldg(rank_base + e) : 0) + rank < C;
+    if (my_kept || !compact) {
+      my_dst = __ldg(offsets + e) + rank;
+      routing_w[my_dst] = my_kept ? gate_w[s] : 0.f;
+      src_idx[my_dst] = t;
+    }
     slot_pos[s] = my_kept ? my_dst : -1;
-    routing_w[my_dst] = my_kept ? gate_w[s] : 0.f;
-    src_idx[my_dst] = t;
   }
   if (permuted == nullptr) return;
   int dst[kMaxTopK];
@@ -443,7 +455,7 @@ __global__ void __launch_bounds__(256)
     }
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
-      if (j < k && (((keptm >> j) & 1u) || fill)) {
+      if (j < k && dst[j] >= 0 && (((keptm >> j) & 1u) || fill)) {
         uint4* o = permuted + size_t(dst[j]) * d8;
         const bool kj = (keptm >> j) & 1u;
 #pragma unroll
@@ -728,20 +740,16 @@ extern "C" size_t lr_route_workspace_bytes(int num_tokens, int top_k, int num_ex
   return route_ws_bytes_for(B < 1 ? 1 : B, num_experts, true);
 }
 
-extern "C" int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, int E,
-                                       int k, int capacity, float load_balance_weight,
-                                       int fill_dropped, int32_t* expert_ids, float* gate_weights,
-                                       int32_t* token_indices, int32_t* offsets,
-                                       int32_t* kept_counts, float* aux_loss, void* permuted,
-                                       float* routing_w, int32_t* source_idx, int32_t* slot_pos,
-                                       void* workspace, size_t workspace_bytes, int32_t* err,
-                                       lr_stream_t stream) {
+extern "C" int lr_topk_route(const float* logits, int T, int E, int k, int capacity,
+                             float load_balance_weight, int32_t* expert_ids, float* gate_weights,
+                             int32_t* token_indices, int32_t* offsets, int32_t* kept_counts,
+                             float* aux_loss, double* prob_sums, int32_t* slot_pos,
+                             void* workspace, size_t workspace_bytes, int32_t* err,
+                             lr_stream_t stream) {
   (void)err;
   if (T <= 0 || E < 1 || E > 64 || k < 1 || k > kMaxTopK || k > E || capacity < 1)
     return LR_ERR_INVALID_ARGUMENT;
-  if (!logits || !expert_ids || !gate_weights || !offsets || !routing_w || !source_idx || !slot_pos)
-    return LR_ERR_INVALID_ARGUMENT;
-  if (permuted && (!x || d <= 0 || d % 8 != 0 || !aligned16(x) || !aligned16(permuted)))
+  if (!logits || !expert_ids || !gate_weights || !offsets || !slot_pos)
     return LR_ERR_INVALID_ARGUMENT;
   const int B = (T + kRouteThreads - 1) / kRouteThreads;
   if (!workspace || workspace_bytes < route_ws_bytes_for(B, E, true)) return LR_ERR_WORKSPACE;
@@ -750,7 +758,7 @@ extern "C" int lr_topk_gating_dispatch(const void* x, const float* logits, int T
 #define LR_ROUTE_CASE(ME)                                                                      \
   topk_route_kernel<ME><<<B, kRouteThreads, 0, stream>>>(                                      \
       logits, T, E, k, capacity, load_balance_weight, expert_ids, gate_weights, token_indices, \
-      slot_pos, offsets, kept_counts, aux_loss, ws, B)
+      slot_pos, offsets, kept_counts, aux_loss, prob_sums, ws, B)
   if (E <= 8)
     LR_ROUTE_CASE(8);
   else if (E <= 16)
@@ -761,13 +769,50 @@ extern "C" int lr_topk_gating_dispatch(const void* x, const float* logits, int T
     LR_ROUTE_CASE(64);
 #undef LR_ROUTE_CASE
   LR_LAUNCH_CHECK();
-  const int pblocks = (T + 7) / 8;
-  permute_tokens_kernel<<<pblocks, 256, 0, stream>>>(
+  return LR_OK;
+}
+
+extern "C" int lr_permute_tokens(const void* x, int T, int d, int E, int k, int capacity,
+                                 const int32_t* expert_ids, const float* gate_weights,
+                                 const int32_t* row_offsets, const int32_t* rank_base,
+                                 int compact, int fill_dropped, int32_t* slot_pos, void* permuted,
+                                 float* routing_w, int32_t* source_idx, const void* workspace,
+                                 size_t workspace_bytes, lr_stream_t stream) {
+  if (T <= 0 || E < 1 || E > 64 || k < 1 || k > kMaxTopK || k > E || capacity < 1)
+    return LR_ERR_INVALID_ARGUMENT;
+  if (!expert_ids || !gate_weights || !row_offsets || !slot_pos || !routing_w || !source_idx)
+    return LR_ERR_INVALID_ARGUMENT;
+  if (permuted && (!x || d <= 0 || d % 8 != 0 || !aligned16(x) || !aligned16(permuted)))
+    return LR_ERR_INVALID_ARGUMENT;
+  const int B = (T + kRouteThreads - 1) / kRouteThreads;
+  if (!workspace || workspace_bytes < route_ws_bytes_for(B, E, true)) return LR_ERR_WORKSPACE;
+  RouteWs ws = carve_route_ws(const_cast<void*>(workspace), B, E, true);
+  permute_tokens_kernel<<<(T + 7) / 8, 256, 0, stream>>>(
       static_cast<const uint4*>(x), T, d / 8, k, E, capacity, fill_dropped, expert_ids,
-      gate_weights, offsets, ws.blk_base, kRouteThreads * k, slot_pos,
+      gate_weights, row_offsets, rank_base, compact, ws.blk_base, kRouteThreads * k, slot_pos,
       static_cast<uint4*>(permuted), routing_w, source_idx);
   LR_LAUNCH_CHECK();
   return LR_OK;
+}
+
+extern "C" int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, int E,
+                                       int k, int capacity, float load_balance_weight,
+                                       int fill_dropped, int32_t* expert_ids, float* gate_weights,
+                                       int32_t* token_indices, int32_t* offsets,
+                                       int32_t* kept_counts, float* aux_loss, void* permuted,
+                                       float* routing_w, int32_t* source_idx, int32_t* slot_pos,
+                                       void* workspace, size_t workspace_bytes, int32_t* err,
+                                       lr_stream_t stream) {
+  if (!routing_w || !source_idx) return LR_ERR_INVALID_ARGUMENT;
+  if (permuted && (!x || d <= 0 || d % 8 != 0 || !aligned16(x) || !aligned16(permuted)))
+    return LR_ERR_INVALID_ARGUMENT;
+  int rc = lr_topk_route(logits, T, E, k, capacity, load_balance_weight, expert_ids, gate_weights,
+                         token_indices, offsets, kept_counts, aux_loss, nullptr, slot_pos,
+                         workspace, workspace_bytes, err, stream);
+  if (rc != LR_OK) return rc;
+  return lr_permute_tokens(x, T, d, E, k, capacity, expert_ids, gate_weights, offsets, nullptr, 0,
+                           fill_dropped, slot_pos, permuted, routing_w, source_idx, workspace,
+                           workspace_bytes, stream);
 }
 
 extern "C" size_t lr_dispatch_workspace_bytes(int num_slots, int num_experts) {

@@ -7,6 +7,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <cstring>
 #include <tuple>
 #include <vector>
@@ -106,6 +107,71 @@ std::vector<at::Tensor> topk_gating_dispatch(const c10::optional<at::Tensor>& x,
                               err_ptr(err), cur_stream()),
       "topk_gating_dispatch");
   return {ids, gw, tok, offsets, kept, aux, permuted, rw, src, pos};
+}
+
+// Phase 1 of the fused dispatch; the returned workspace must be passed to permute_tokens.
+std::vector<at::Tensor> topk_route(const at::Tensor& logits, int64_t k, int64_t capacity,
+                                   double lbw, const c10::optional<at::Tensor>& err) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.scalar_type() == at::kFloat, "logits: (T,E) fp32");
+  const int64_t T = logits.size(0), E = logits.size(1), S = T * k;
+  c10::cuda::CUDAGuard g(logits.device());
+  auto iopt = logits.options().dtype(at::kInt);
+  auto fopt = logits.options().dtype(at::kFloat);
+  auto ids = at::empty({S}, iopt);
+  auto gw = at::empty({S}, fopt);
+  auto tok = at::empty({S}, iopt);
+  auto offsets = at::empty({E + 1}, iopt);
+  auto kept = at::empty({E}, iopt);
+  auto aux = at::zeros({}, fopt);
+  auto psum = at::empty({E}, logits.options().dtype(at::kDouble));
+  auto pos = at::empty({S}, iopt);
+  auto ws = workspace(lr_route_workspace_bytes(int(T), int(k), int(E)), logits);
+  check_status(lr_topk_route(logits.data_ptr<float>(), int(T), int(E), int(k), int(capacity),
+                             float(lbw), ids.data_ptr<int32_t>(), gw.data_ptr<float>(),
+                             tok.data_ptr<int32_t>(), offsets.data_ptr<int32_t>(),
+                             kept.data_ptr<int32_t>(), aux.data_ptr<float>(),
+                             psum.data_ptr<double>(), pos.data_ptr<int32_t>(), ws.data_ptr(),
+                             size_t(ws.numel()), err_ptr(err), cur_stream()),
+               "topk_route");
+  return {ids, gw, tok, offsets, kept, aux, psum, pos, ws};
+}
+
+// Phase 2: rows for kept slots (rank_base / compact as in lr_permute_tokens).
+// slot_pos is updated in place from block ranks to rows.
+std::vector<at::Tensor> permute_tokens(const at::Tensor& x, const at::Tensor& expert_ids,
+                                       const at::Tensor& gate_weights,
+                                       const at::Tensor& row_offsets,
+                                       const c10::optional<at::Tensor>& rank_base,
+                                       int64_t capacity, bool compact, bool fill_dropped,
+                                       at::Tensor slot_pos, const at::Tensor& ws,
+                                       int64_t num_rows, int64_t num_experts) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.scalar_type() == at::kHalf, "x: (T,d) fp16");
+  const int64_t T = x.size(0), S = expert_ids.numel(), k = S / std::max<int64_t>(T, 1);
+  TORCH_CHECK(k * T == S, "slot count must be T*k");
+  TORCH_CHECK(row_offsets.numel() == num_experts + 1, "row_offsets: (E+1,)");
+  c10::cuda::CUDAGuard g(x.device());
+  auto iopt = x.options().dtype(at::kInt);
+  auto permuted = at::empty({num_rows, x.size(1)}, x.options());
+  auto rw = at::empty({std::max<int64_t>(num_rows, 1)}, x.options().dtype(at::kFloat));
+  auto src = at::empty({std::max<int64_t>(num_rows, 1)}, iopt);
+  const int32_t* rb = nullptr;
+  if (rank_base.has_value() && rank_base->defined()) {
+    check_cuda(*rank_base, "rank_base");
+    TORCH_CHECK(rank_base->numel() == num_experts, "rank_base: (E,)");
+    rb = rank_base->data_ptr<int32_t>();
+  }
+  check_status(lr_permute_tokens(x.data_ptr(), int(T), int(x.size(1)), int(num_experts), int(k),
+                                 int(capacity), expert_ids.data_ptr<int32_t>(),
+                                 gate_weights.data_ptr<float>(), row_offsets.data_ptr<int32_t>(),
+                                 rb, compact ? 1 : 0, fill_dropped ? 1 : 0,
+                                 slot_pos.data_ptr<int32_t>(),
+                                 num_rows ? permuted.data_ptr() : nullptr, rw.data_ptr<float>(),
+                                 src.data_ptr<int32_t>(), ws.data_ptr(), size_t(ws.numel()),
+                                 cur_stream()),
+               "permute_tokens");
+  return {permuted, rw, src};
 }
 
 std::vector<at::Tensor> expert_routing_forward(const at::Tensor& tokens,
@@ -280,6 +346,12 @@ TORCH_LIBRARY(lightning_router, m) {
       "expert_routing_forward(Tensor tokens, Tensor expert_ids, Tensor gate_weights, "
       "Tensor token_indices, int num_experts, int capacity, bool fill_dropped, Tensor? err) -> "
       "Tensor[]");
+  m.def(
+      "topk_route(Tensor logits, int k, int capacity, float lbw, Tensor? err) -> Tensor[]");
+  m.def(
+      "permute_tokens(Tensor x, Tensor expert_ids, Tensor gate_weights, Tensor row_offsets, "
+      "Tensor? rank_base, int capacity, bool compact, bool fill_dropped, Tensor(a!) slot_pos, "
+      "Tensor ws, int num_rows, int num_experts) -> Tensor[]");
   m.def("combine(Tensor y, Tensor gate_weights, Tensor slot_pos, int num_tokens, int k) -> Tensor");
   m.def(
       "expert_routing_gather(Tensor expert_output, Tensor routing_weights, Tensor "
@@ -297,6 +369,8 @@ TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
   m.impl("topk_gating_dispatch", &topk_gating_dispatch);
   m.impl("expert_routing_forward", &expert_routing_forward);
   m.impl("combine", &combine);
+  m.impl("topk_route", &topk_route);
+  m.impl("permute_tokens", &permute_tokens);
   m.impl("expert_routing_gather", &expert_routing_gather);
   m.impl("grouped_w4a16_gemm", &grouped_w4a16_gemm);
 }

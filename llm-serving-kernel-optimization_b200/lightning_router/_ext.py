@@ -24,6 +24,7 @@ C_ABI_SYMBOLS = (
     "lr_status_string", "lr_abi_version", "lr_last_cuda_error",
     "lr_gate_logits",
     "lr_route_workspace_bytes", "lr_topk_gating_dispatch", "lr_topk_gating_dispatch_noalloc",
+    "lr_topk_route", "lr_permute_tokens",
     "lr_dispatch_workspace_bytes", "lr_expert_routing_forward",
     "lr_combine", "lr_gather_workspace_bytes", "lr_expert_routing_gather",
     "lr_weight_table_bytes", "lr_encode_weight_table",

@@ -1,0 +1,168 @@
+"""Expert-parallel exchange logic on CPU ``gloo`` ranks (no GPU).
+
+Each rank routes its token shard with the oracle's gating, applies the global
+slot-order capacity through ``plan_exchange``, exchanges kept rows with
+``all_to_all_single``, runs its local experts (oracle FFN), returns the rows
+and combines.  The gathered result must equal the single-process oracle:
+routing (kept slots) exactly, outputs to fp32 rounding.
+
+A second test makes a rank fail on the host before the exchange and checks
+that the surviving rank's collective ends with an error within the process
+group timeout instead of waiting forever.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle as orc
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(T, d, f, E, k, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, d)).astype(np.float16)
+    logits = (rng.standard_normal((T, E)) + np.linspace(1.0, -1.0, E)).astype(np.float32)
+    experts = []
+    for _ in range(E):
+        experts.append({
+            "gate": (rng.standard_normal((d, f)) * 0.05).astype(np.float16),
+            "up": (rng.standard_normal((d, f)) * 0.05).astype(np.float16),
+            "down": (rng.standard_normal((f, d)) * 0.05).astype(np.float16),
+        })
+    return x, logits, experts
+
+
+def _rank_main(rank, world, port, cfg, q):
+    try:
+        from lightning_router.serving.ep import plan_exchange
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=30))
+        T, d, f, E, k, cf, seed = cfg
+        x, logits, experts = _problem(T, d, f, E, k, seed)
+        Tl = T // world
+        xs, ls = x[rank * Tl:(rank + 1) * Tl], logits[rank * Tl:(rank + 1) * Tl]
+        ids, w, probs = orc.topk_gating(ls, k)
+        ids, w = ids.reshape(-1), w.reshape(-1)
+        counts = np.bincount(ids, minlength=E)
+        stats_l = np.concatenate([[Tl], counts, probs.astype(np.float64).sum(0)]).astype(np.float64)
+        stats = torch.zeros(world * (1 + 2 * E), dtype=torch.float64)
+        dist.all_gather_into_tensor(stats, torch.from_numpy(stats_l))
+        plan = plan_exchange(stats.view(world, -1).numpy(), rank, world, E, k, cf, 0.01)
+        # local slot ranks in slot order, kept iff base + rank < C, compact rows
+        order = np.argsort(ids, kind="stable")
+        local_rank = np.empty_like(ids)
+        starts = np.concatenate([[0], np.cumsum(counts)])
+        local_rank[order] = np.arange(ids.size) - starts[ids[order]]
+        kept = plan.rank_base[ids] + local_rank < plan.capacity
+        send = np.zeros((plan.n_send, d), np.float16)
+        pos = np.full(ids.size, -1, np.int64)
+        tok = np.repeat(np.arange(Tl), k)
+        for s in np.nonzero(kept)[0]:
+            pos[s] = plan.koff[ids[s]] + local_rank[s]
+            send[pos[s]] = xs[tok[s]]
+        recv = torch.zeros(plan.n_recv, d, dtype=torch.float16)
+        dist.all_to_all_single(recv, torch.from_numpy(send), plan.recv_rows, plan.send_rows)
+        rr = recv.numpy()
+        a = rr[plan.reorder] if plan.reorder is not None else rr
+        El = E // world
+        y = np.zeros((plan.n_recv, d), np.float32)
+        for el in range(El):
+            st, n = int(plan.seg_start[el]), int(plan.seg_len[el])
+            if n:
+                ex = experts[rank * El + el]
+                y[st:st + n] = orc.expert_ffn(a[st:st + n], ex["up"], ex["down"], ex["gate"])
+        if plan.reorder is not None:
+            y_send = np.empty_like(y)
+            y_send[plan.reorder] = y
+        else:
+            y_send = y
+        back = torch.zeros(plan.n_send, d, dtype=torch.float32)
+        dist.all_to_all_single(back, torch.from_numpy(y_send), plan.send_rows, plan.recv_rows)
+        bk = back.numpy()
+        out = np.zeros((Tl, d), np.float32)
+        for s in np.nonzero(kept)[0]:
+            out[tok[s]] += w[s] * bk[pos[s]]
+        full = [torch.zeros(Tl, d) for _ in range(world)]
+        dist.all_gather(full, torch.from_numpy(out))
+        kept_all = [torch.zeros(Tl * k, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(kept_all, torch.from_numpy(kept.astype(np.int64)))
+        if rank == 0:
+            q.put(("ok", torch.cat(full).numpy(), torch.cat(kept_all).numpy(), plan.aux_loss))
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("err", traceback.format_exc(), None, None))
+
+
+@pytest.mark.parametrize("world,E,k,cf", [(2, 4, 2, 1.0), (2, 8, 2, 1.25), (4, 8, 3, 0.75),
+                                          (2, 2, 1, 2.0)])
+def test_ep_exchange_matches_single_process_oracle(world, E, k, cf):
+    T, d, f = 48 * world, 32, 48
+    cfg = (T, d, f, E, k, cf, 1234 + world + E)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cfg, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "ok", res[1]
+    _, got, kept_got, aux_got = res
+    x, logits, experts = _problem(T, d, f, E, k, cfg[-1])
+    ref, aux, r = orc.moe_layer(x, logits, k, cf, experts)
+    np.testing.assert_array_equal(kept_got.astype(bool), r.kept)
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+    assert abs(aux_got - aux) <= 1e-9 + 1e-7 * abs(aux)
+
+
+def _failing_rank(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=4))
+        if rank == 1:
+            raise SystemExit(3)  # host-side failure before the exchange
+        t = torch.zeros(4)
+        try:
+            dist.all_to_all_single(t, torch.ones(4), [2, 2], [2, 2])
+            q.put(("no-error", None))
+        except Exception as e:  # the peer is gone: the collective must fail, not hang
+            q.put(("error", type(e).__name__))
+    except SystemExit:
+        raise
+    except Exception:
+        q.put(("setup-error", traceback.format_exc()))
+
+
+def test_dead_rank_is_detected_by_timeout():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    status, info = q.get(timeout=90)
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert status == "error", (status, info)

@@ -1,0 +1,87 @@
+"""Expert-parallel layer on 2+ GPUs (NCCL) against the single-GPU layer.
+
+Each rank builds the same seeded layer, runs ``ExpertParallelMoE.forward`` on
+its token shard, and rank 0 compares the gathered output with
+``MoELayer.forward`` on the whole batch: bit-identical (every kept row goes
+through the same kernels and the combine sums in the same slot order), with
+the same routing and an aux loss equal to 1e-6 relative.  Skipped when fewer
+GPUs than ranks are visible.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, wname, overrides, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        from lightning_router.serving.ep import ExpertParallelMoE
+        from lightning_router.workloads import WORKLOADS, build_layer
+        w = dataclasses.replace(WORKLOADS[wname], **overrides)
+        layer, t = build_layer(w, device=dev)
+        Tl = w.tokens // world
+        ep = ExpertParallelMoE.from_layer(layer, world, rank)
+        out, aux = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
+        out2, _ = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
+        same = bool(torch.equal(out, out2))
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out)
+        if rank == 0:
+            ref, ref_aux = layer(t.x)
+            full = torch.cat(gathered)
+            q.put(("ok", bool(torch.equal(full, ref)), float((full.float() - ref.float()).abs().max()),
+                   float(aux), float(ref_aux), same))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("err", traceback.format_exc(), None, None, None, None))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("wname,overrides", [
+    ("prefill", dict(tokens=2048, d_model=1024, d_ff=2048)),
+    ("fine", dict(tokens=1024, d_model=512)),
+])
+def test_expert_parallel_matches_single_gpu(world, wname, overrides):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, wname, overrides, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert res[0] == "ok", res[1]
+    _, equal, maxdiff, aux, ref_aux, repeat_same = res
+    assert repeat_same
+    assert equal, f"EP output differs from single GPU (max |diff| {maxdiff})"
+    assert abs(aux - ref_aux) <= 1e-6 * abs(ref_aux)
