@@ -230,8 +230,10 @@ def stage_times(events, steps):
 
 
 def run_gpu(args, ws, rank, local):
-    from lightning_router.workloads import WORKLOADS, build_layer, ffn_flops
+    from lightning_router.workloads import WORKLOADS, build_layer
     w = WORKLOADS[args.workload]
+    if args.tokens:
+        w = dataclasses.replace(w, tokens=args.tokens)
     dev = torch.device("cuda", local)
     peaks, peak_kind = _peaks()
 
@@ -261,7 +263,8 @@ def run_gpu(args, ws, rank, local):
     torch.cuda.synchronize()
     barrier(ws)
 
-    # timed region (device time, max over ranks)
+    # timed region (device time, max over ranks).  cudaProfilerStart/Stop bracket
+    # it so `ncu --profile-from-start off` lists exactly the timed launches.
     stage_owner.stage_events = []
     clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
                           else local)
@@ -271,11 +274,13 @@ def run_gpu(args, ws, rank, local):
     barrier(ws)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     wall0 = time.perf_counter()
+    torch.cuda.cudart().cudaProfilerStart()
     start.record()
     for _ in range(args.steps):
         fwd(x)
     end.record()
     torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
     wall = time.perf_counter() - wall0
     barrier(ws)
     clk = clocks.stop()
@@ -353,9 +358,74 @@ def run_gpu(args, ws, rank, local):
     return result
 
 
+def run_sweep(args, ws, rank, local):
+    """Dispatch/combine sweep (routing kernels only): HBM GB/s against the measured copy peak.
+
+    Each step is one fused top-k gating + dispatch (route + permute kernels) from given
+    fp32 logits, then one combine with identity experts.  L2 is flushed between steps
+    (a 512 MiB write outside the timed events).
+    """
+    from lightning_router.kernels.expert_routing import combine, topk_gating_dispatch
+    from lightning_router.workloads import (SWEEP_D, SWEEP_E, SWEEP_K, SWEEP_TOKENS,
+                                            combine_bytes, dispatch_bytes, sweep_inputs)
+    dev = torch.device("cuda", local)
+    peaks, peak_kind = _peaks()
+    hbm = float(peaks["hbm_gbs"])
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    tokens = SWEEP_TOKENS if args.tokens is None else (args.tokens,)
+    rows = []
+    for cf in (1.0, 2.0):
+        for i, T in enumerate(tokens):
+            x, logits = sweep_inputs(T, SWEEP_TOKENS.index(T) if T in SWEEP_TOKENS else 0,
+                                     device=dev, gen_device=dev)
+            times = {"dispatch": [], "combine": []}
+            plan = None
+            for it in range(args.warmup + args.steps):
+                flush.zero_()
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                e[0].record()
+                plan = topk_gating_dispatch(x, logits, SWEEP_K, cf, fill_dropped=False)
+                e[1].record()
+                out = combine(plan.permuted, plan.gate_weights, plan.slot_pos, T, SWEEP_K)
+                e[2].record()
+                torch.cuda.synchronize()
+                if it >= args.warmup:
+                    times["dispatch"].append(e[0].elapsed_time(e[1]))
+                    times["combine"].append(e[1].elapsed_time(e[2]))
+            kept = int(plan.kept_counts.sum())
+            S = T * SWEEP_K
+            db = dispatch_bytes(T, SWEEP_D, SWEEP_E, S, kept)
+            cb = combine_bytes(T, SWEEP_D, S, kept)
+            dms = statistics.median(times["dispatch"])
+            cms = statistics.median(times["combine"])
+            rows.append({"tokens": T, "cf": cf, "kept_slots": kept,
+                         "dispatch_ms": dms, "dispatch_gbs": db / dms / 1e6,
+                         "combine_ms": cms, "combine_gbs": cb / cms / 1e6,
+                         "dispatch_bytes": db, "combine_bytes": cb})
+            del x, logits, plan, out
+    head = max(rows, key=lambda r: (r["tokens"], -r["cf"]))
+    head = [r for r in rows if r["tokens"] == head["tokens"] and r["cf"] == 1.0][0]
+    return {
+        "metric": "dispatch HBM GB/s", "value": head["dispatch_gbs"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head["dispatch_ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"dispatch/combine sweep: d_model {SWEEP_D}, {SWEEP_E} experts "
+                               f"top-{SWEEP_K}, logits N(0,1) given; headline T={head['tokens']} "
+                               "cf 1.0", "l2": "flushed between steps (512 MiB write)"},
+        "roofline": {"kernel": "route + permute (dispatch)", "bound": "hbm",
+                     "achieved": head["dispatch_gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": head["dispatch_gbs"] / hbm, "peak_kind": f"{peak_kind} copy",
+                     "traffic": None, "combine_gbs": head["combine_gbs"],
+                     "combine_frac": head["combine_gbs"] / hbm},
+        "sweep": rows,
+        "gpu_launches": 3 * args.steps * len(rows),
+    }
+
+
 def run_reference(args, ws, rank):
     from lightning_router.workloads import WORKLOADS
-    w = WORKLOADS[args.workload]
+    w = WORKLOADS["prefill" if args.workload == "sweep" else args.workload]
     if rank != 0:
         return None
     v, desc, cores = run_cpu(w, steps=max(1, args.steps), warmup=min(args.warmup, 1),
@@ -377,7 +447,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="prefill",
-                    choices=["prefill", "decode", "pr1", "fine"])
+                    choices=["prefill", "decode", "pr1", "fine", "sweep"])
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override the token count (smaller profiling cases)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     args = ap.parse_args()
@@ -387,6 +459,8 @@ def main():
     try:
         if args.impl == "reference":
             res = run_reference(args, ws, rank)
+        elif args.workload == "sweep":
+            res = run_sweep(args, ws, rank, local)
         else:
             res = run_gpu(args, ws, rank, local)
         if rank == 0 and res is not None:

@@ -93,24 +93,50 @@ LR_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: spins on try_wait until the phase with `parity` completes,
-// `*abort` becomes non-zero, or `limit_ns` elapses.  Returns true when the
-// phase completed.  On a timeout it raises `*abort` (shared) and the device
-// error word so every role of the CTA drains and exits.
+// Non-blocking test of a phase (acquire on success).  Its result is consumed
+// later, so its latency can overlap other work of the issuing thread.
+LR_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is
+// incomplete (it returns as soon as the phase completes), so waiting warps do
+// not take issue slots from working ones.
+LR_DEVICE bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: waits (suspending, see mbar_try_wait_hint) until the phase with
+// `parity` completes, `*abort` becomes non-zero, or `limit_ns` elapses.  Returns
+// true when the phase completed.  On a timeout it raises `*abort` (shared) and
+// the device error word so every role of the CTA drains and exits.
 LR_DEVICE bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
                                  int32_t* err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (((++spins) & 63u) == 0) {
-      if (*abort) return false;
-      if (global_timer_ns() - t0 > limit_ns) {
-        *abort = 1;
-        report(err, LR_DEVERR_PIPE_TIMEOUT);
-        return false;
-      }
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      *abort = 1;
+      report(err, LR_DEVERR_PIPE_TIMEOUT);
+      return false;
     }
   }
 }

@@ -74,20 +74,26 @@ LR_DEVICE void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uin
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(128) gate_logits_kernel(const __half* __restrict__ h,
-                                                          const __half* __restrict__ wg,
-                                                          const float* __restrict__ bias, int T,
-                                                          int d, int E, int n_egroups,
-                                                          float* __restrict__ logits) {
-  const int warp_global = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int tile = warp_global / n_egroups;
-  const int eg = warp_global % n_egroups;
+// One block per (16-token tile, 32-expert group).  Its 8 warps split d into
+// 8 contiguous chunks (each a multiple of 16), accumulate 16x32 partial logits
+// with mma.sync, and the partials are summed in warp order through shared
+// memory (deterministic), so small token counts still spread over many warps.
+constexpr int kGateWarps = 8;
+
+__global__ void __launch_bounds__(kGateWarps * 32)
+    gate_logits_kernel(const __half* __restrict__ h, const __half* __restrict__ wg,
+                       const float* __restrict__ bias, int T, int d, int E, int n_egroups,
+                       float* __restrict__ logits) {
+  __shared__ float red[kGateWarps][16][33];
+  const int tile = blockIdx.x / n_egroups;
+  const int eg = blockIdx.x % n_egroups;
   const int t0 = tile * 16;
-  if (t0 >= T) return;
-  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int e0 = eg * 32;
   const int row0 = t0 + g, row1 = t0 + g + 8;
   const bool r0 = row0 < T, r1 = row1 < T;
+  const int kc = ((d / 16 + kGateWarps - 1) / kGateWarps) * 16;
+  const int kbeg = warp * kc, kend = min(d, kbeg + kc);
   const __half* h0 = h + size_t(r0 ? row0 : 0) * d + 2 * tq;
   const __half* h1 = h + size_t(r1 ? row1 : 0) * d + 2 * tq;
   const __half* wrow[4];
@@ -104,7 +110,8 @@ __global__ void __launch_bounds__(128) gate_logits_kernel(const __half* __restri
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
 
-  for (int k0 = 0; k0 < d; k0 += 16) {
+#pragma unroll 2
+  for (int k0 = kbeg; k0 < kend; k0 += 16) {
     uint32_t a[4];
     a[0] = r0 ? ld_u32(h0 + k0) : 0u;
     a[1] = r1 ? ld_u32(h1 + k0) : 0u;
@@ -120,17 +127,19 @@ __global__ void __launch_bounds__(128) gate_logits_kernel(const __half* __restri
     }
   }
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    const int c0 = e0 + nt * 8 + 2 * tq;
+  for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = (i < 2) ? row0 : row1;
-      const int col = c0 + (i & 1);
-      if (row < T && col < E) {
-        float v = acc[nt][i];
-        if (bias) v += bias[col];
-        logits[size_t(row) * E + col] = v;
-      }
+    for (int i = 0; i < 4; ++i) red[warp][(i < 2) ? g : g + 8][nt * 8 + 2 * tq + (i & 1)] = acc[nt][i];
+  __syncthreads();
+  for (int o = threadIdx.x; o < 16 * 32; o += kGateWarps * 32) {
+    const int rr = o >> 5, cc = o & 31;
+    const int row = t0 + rr, col = e0 + cc;
+    if (row < T && col < E) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGateWarps; ++w) v += red[w][rr][cc];
+      if (bias) v += bias[col];
+      logits[size_t(row) * E + col] = v;
     }
   }
 }
@@ -725,9 +734,8 @@ extern "C" int lr_gate_logits(const void* h, const void* wg, const float* bias, 
   if (T == 0) return LR_OK;
   if (!h || !wg || !logits) return LR_ERR_INVALID_ARGUMENT;
   const int n_eg = (E + 31) / 32;
-  const long warps = long((T + 15) / 16) * n_eg;
-  const int blocks = int((warps + 3) / 4);
-  gate_logits_kernel<<<blocks, 128, 0, stream>>>(static_cast<const __half*>(h),
+  const long blocks = long((T + 15) / 16) * n_eg;
+  gate_logits_kernel<<<unsigned(blocks), kGateWarps * 32, 0, stream>>>(static_cast<const __half*>(h),
                                                  static_cast<const __half*>(wg), bias, T, d, E,
                                                  n_eg, logits);
   LR_LAUNCH_CHECK();

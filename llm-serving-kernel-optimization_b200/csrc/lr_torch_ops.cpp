@@ -79,7 +79,7 @@ std::vector<at::Tensor> topk_gating_dispatch(const c10::optional<at::Tensor>& x,
   auto tok = at::empty({S}, iopt);
   auto offsets = at::empty({E + 1}, iopt);
   auto kept = at::empty({E}, iopt);
-  auto aux = at::zeros({}, fopt);
+  auto aux = with_aux ? at::empty({}, fopt) : at::zeros({}, fopt);  // the kernel writes it
   auto rw = at::empty({S}, fopt);
   auto src = at::empty({S}, iopt);
   auto pos = at::empty({S}, iopt);
@@ -123,7 +123,7 @@ std::vector<at::Tensor> topk_route(const at::Tensor& logits, int64_t k, int64_t 
   auto tok = at::empty({S}, iopt);
   auto offsets = at::empty({E + 1}, iopt);
   auto kept = at::empty({E}, iopt);
-  auto aux = at::zeros({}, fopt);
+  auto aux = at::empty({}, fopt);
   auto psum = at::empty({E}, logits.options().dtype(at::kDouble));
   auto pos = at::empty({S}, iopt);
   auto ws = workspace(lr_route_workspace_bytes(int(T), int(k), int(E)), logits);

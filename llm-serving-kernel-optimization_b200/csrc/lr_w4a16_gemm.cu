@@ -8,15 +8,16 @@
 // in tensor memory (128 lanes = features, BN fp32 columns = tokens), double
 // buffered so the epilogue of one tile overlaps the main loop of the next.
 //
-// Warp roles (448 threads, one CTA per SM, persistent over tiles):
-//   warps 0-3   epilogue: tcgen05.ld -> activation -> fp16 -> staged in smem
-//               -> coalesced 16-byte stores (rows clipped to the expert segment)
-//   warps 4-11  dequant: packed int32 words (TMA-staged) -> 8 fp16 each,
+// Warp roles (576 threads, one CTA per SM, persistent over tiles):
+//   warps 0-7   epilogue (two groups of four, alternate 16-token chunks):
+//               tcgen05.ld -> activation -> fp16 -> staged in smem -> coalesced
+//               16-byte stores (rows clipped to the expert segment)
+//   warps 8-15  dequant: packed int32 words (TMA-staged) -> 8 fp16 each,
 //               fp16(scale * (q - zero)) computed exactly, written into the
 //               128-byte-swizzled MN-major operand buffer
-//   warp 12     producer: TMA tile loads of tokens and packed weights, bulk
-//               copies of the per-group scales / zeros
-//   warp 13     TMEM allocation + single-thread tcgen05.mma issue
+//   warp 16     producer: TMA tile loads of tokens and packed weights (the
+//               dequant warps read the per-group scales / zeros themselves)
+//   warp 17     TMEM allocation + single-thread tcgen05.mma issue
 //
 // Every mbarrier wait is bounded in time; a wait that runs out raises a
 // shared abort flag and LR_DEVERR_PIPE_TIMEOUT so all roles drain and exit.
@@ -42,32 +43,28 @@ struct alignas(128) ExpertEntry {
 };
 static_assert(sizeof(ExpertEntry) % 128 == 0, "table entry alignment");
 
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;
 constexpr int kDeqWarps = 8;
 constexpr int kProdWarp = kEpiWarps + kDeqWarps;
 constexpr int kMmaWarp = kProdWarp + 1;
 constexpr int kGemmThreads = (kMmaWarp + 1) * 32;
 constexpr int kBK = 64;
-constexpr int kDStages = 2;
 constexpr int kMaxGemmExperts = 256;
 constexpr int kABytes = 128 * kBK * 2;      // dequantized operand, one buffer
 constexpr int kWBytes = kBK * 16 * 4;       // packed weights per stage (128 features)
-constexpr int kSBytes = 128 * 2;            // scales per stage
-constexpr int kZBytes = 16 * 4;             // zeros per stage
-constexpr int kCBytes = 12288;              // epilogue staging
+constexpr int kCBytes = 6144;               // epilogue staging: [16][128] fp16, or [16][64] fp32 + [16][64] fp16
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 constexpr uint64_t kDrainLimitNs = 100000000ull;  // 100 ms
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int DSTAGES>
 struct GemmLayout {
+  static constexpr int kDStages = DSTAGES;
   static constexpr int kBStage = BN * 128;
   static constexpr int offB = 0;
   static constexpr int offA = offB + STAGES * kBStage;
   static constexpr int offW = offA + kDStages * kABytes;
-  static constexpr int offS = offW + STAGES * kWBytes;
-  static constexpr int offZ = offS + STAGES * kSBytes;
-  static constexpr int offC = offZ + STAGES * kZBytes;
-  static constexpr int offBar = offC + kCBytes;
+  static constexpr int offC = offW + STAGES * kWBytes;
+  static constexpr int offBar = offC + 2 * kCBytes;
   static constexpr int kNumBars = 2 * STAGES + 2 * kDStages + 4 + 1;
   static constexpr int offMisc = offBar + kNumBars * 8;
   static constexpr int kMiscInts = 8;
@@ -77,18 +74,21 @@ struct GemmLayout {
   static_assert(offA % 1024 == 0, "operand alignment");
 };
 
+// Pipeline depths per token tile: v = TMA stages (tokens + packed weights),
+// d = dequantized-operand buffers.  Small tiles do little tensor work per k-step,
+// so the dequant -> MMA -> release chain must be deeper to hide its latency.
 template <int BN>
 struct GemmStages;
 template <>
-struct GemmStages<16> { static constexpr int v = 16; };
+struct GemmStages<16> { static constexpr int v = 16, d = 4; };
 template <>
-struct GemmStages<32> { static constexpr int v = 16; };
+struct GemmStages<32> { static constexpr int v = 16, d = 4; };
 template <>
-struct GemmStages<64> { static constexpr int v = 12; };
+struct GemmStages<64> { static constexpr int v = 10, d = 4; };
 template <>
-struct GemmStages<128> { static constexpr int v = 8; };
+struct GemmStages<128> { static constexpr int v = 8, d = 2; };
 template <>
-struct GemmStages<256> { static constexpr int v = 4; };
+struct GemmStages<256> { static constexpr int v = 4, d = 2; };
 
 // ---------------------------------------------------------------------------
 // int4 -> fp16 dequantization of one packed word (8 features)
@@ -131,20 +131,38 @@ LR_DEVICE void deq_params(uint32_t zword, uint4 sc, DeqParams& P) {
 }
 
 // fp16(scale * (q - z)): (1024+q) - (1024+z) is exact in fp16, and the product
-// of an fp16 scale with an integer in [-15, 15] is rounded once.
+// of an fp16 scale with an integer in [-15, 15] is rounded once.  The eight
+// halves come out in the order f0 f4 f1 f5 f2 f6 f3 f7; the operand keeps that
+// order (a permutation of the tile's M rows) and the epilogue maps each
+// accumulator lane back to its feature with lane_feature().
 LR_DEVICE uint4 deq_word(uint32_t w, const DeqParams& P) {
-  uint32_t r[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) r[p] = h2_mul(h2_sub(nib_pair(w, p), P.z[p]), P.s[p]);
   uint4 o;
-  o.x = prmt(r[0], r[1], 0x5410);  // f0 f1
-  o.y = prmt(r[2], r[3], 0x5410);  // f2 f3
-  o.z = prmt(r[0], r[1], 0x7632);  // f4 f5
-  o.w = prmt(r[2], r[3], 0x7632);  // f6 f7
+  o.x = h2_mul(h2_sub(nib_pair(w, 0), P.z[0]), P.s[0]);
+  o.y = h2_mul(h2_sub(nib_pair(w, 1), P.z[1]), P.s[1]);
+  o.z = h2_mul(h2_sub(nib_pair(w, 2), P.z[2]), P.s[2]);
+  o.w = h2_mul(h2_sub(nib_pair(w, 3), P.z[3]), P.s[3]);
   return o;
 }
 
-LR_DEVICE void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Feature (within its 8-feature group) held by accumulator lane `lane`.
+LR_DEVICE int lane_feature(int lane) { return (lane & ~7) | ((lane & 7) >> 1) | ((lane & 1) << 2); }
+
+// Named barrier over the 128 threads of one epilogue group.
+LR_DEVICE void named_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// Named barrier that also returns whether any of the 128 threads passed `pred`.
+LR_DEVICE bool named_bar_any(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.or.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(id)
+      : "memory");
+  return r != 0;
+}
 
 LR_DEVICE bool wait_any(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
   return mbar_wait_bounded(bar, parity, abort, err, kWaitLimitNs);
@@ -161,22 +179,21 @@ LR_DEVICE void wait_drain(uint64_t* bar, uint32_t parity) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int DSTAGES, int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a16_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const ExpertEntry* __restrict__ table, int E, int mat, int K, int N,
                               const int32_t* __restrict__ seg_start,
                               const int32_t* __restrict__ seg_len, int max_rows, int R,
                               __half* __restrict__ C, int32_t* err) {
-  using L = GemmLayout<BN, STAGES>;
+  using L = GemmLayout<BN, STAGES, DSTAGES>;
+  constexpr int kDStages = DSTAGES;
   constexpr int BO = (MODE == LR_FFN_MODE_SWIGLU) ? 64 : 128;  // output features per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sB = smem + L::offB;
   uint8_t* sA = smem + L::offA;
   uint32_t* sW = reinterpret_cast<uint32_t*>(smem + L::offW);
-  __half* sS = reinterpret_cast<__half*>(smem + L::offS);
-  uint32_t* sZ = reinterpret_cast<uint32_t*>(smem + L::offZ);
   uint8_t* sC = smem + L::offC;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::offBar);
   uint64_t* empty = full + STAGES;
@@ -188,7 +205,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int* misc = reinterpret_cast<int*>(smem + L::offMisc);
   volatile int* s_abort = misc;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 1);
-  volatile int* s_epi_fail = misc + 2;
   int* s_tbase = reinterpret_cast<int*>(smem + L::offTab);  // E+1
   int* s_start = s_tbase + E + 1;                            // E
   int* s_len = s_start + E;                                  // E
@@ -204,7 +220,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < kDStages; ++i) {
-      mbar_init(&dfull[i], kDeqWarps);
+      mbar_init(&dfull[i], kDeqWarps / kDStages);
       mbar_init(&dempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -213,7 +229,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(fin, 1);
     *s_abort = 0;
-    *s_epi_fail = 0;
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
@@ -293,27 +308,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const ExpertEntry* ent = table + e;
         const int row0 = s_start[e] + mt * BN;
         const int n0 = nt * BO;
-        const int g = ent->group_size;
-        const int m0 = (MODE == LR_FFN_MODE_SWIGLU) ? 0 : mat;
         const CUtensorMap* wmap0 = (MODE == LR_FFN_MODE_SWIGLU) ? &ent->qw8[0] : &ent->qw16[mat];
         const CUtensorMap* wmap1 = &ent->qw8[1];
-        const __half* sc0 = ent->scales[m0];
-        const __half* sc1 = ent->scales[1];
-        const int32_t* z0 = ent->zeros[m0];
-        const int32_t* z1 = ent->zeros[1];
         // descriptors were written to global memory by a copy before the launch
         tensormap_acquire(wmap0);
         if (MODE == LR_FFN_MODE_SWIGLU) tensormap_acquire(wmap1);
-        int sbytes, zbytes;
-        if (MODE == LR_FFN_MODE_SWIGLU) {
-          sbytes = 256;
-          zbytes = 64;
-        } else {
-          const int feat = min(128, N - n0);
-          sbytes = feat * 2;
-          zbytes = (feat / 8) * 4;
-        }
-        const uint32_t tx = uint32_t(BN * 128 + kWBytes + sbytes + zbytes);
+        // Only the token box and the packed weight box(es) travel by TMA: each
+        // copy costs issue time on this single thread, so the small per-group
+        // scale / zero rows are read by the dequant warps themselves.
+        const uint32_t tx = uint32_t(BN * 128 + kWBytes);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -323,22 +326,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           mbar_arrive_expect_tx(&full[s], tx);
           tma_load_2d(sB + s * L::kBStage, &tmap_a, &full[s], kb * kBK, row0);
-          const size_t grow = size_t((kb * kBK) / g);
           uint32_t* w = sW + s * (kWBytes / 4);
-          __half* ss = sS + s * (kSBytes / 2);
-          uint32_t* zz = sZ + s * (kZBytes / 4);
-          if (MODE == LR_FFN_MODE_SWIGLU) {
-            tma_load_2d(w, wmap0, &full[s], n0 / 8, kb * kBK);
-            tma_load_2d(w + 512, wmap1, &full[s], n0 / 8, kb * kBK);
-            bulk_load(ss, sc0 + grow * N + n0, 128, &full[s]);
-            bulk_load(ss + 64, sc1 + grow * N + n0, 128, &full[s]);
-            bulk_load(zz, z0 + grow * (N / 8) + n0 / 8, 32, &full[s]);
-            bulk_load(zz + 8, z1 + grow * (N / 8) + n0 / 8, 32, &full[s]);
-          } else {
-            tma_load_2d(w, wmap0, &full[s], n0 / 8, kb * kBK);
-            bulk_load(ss, sc0 + grow * N + n0, sbytes, &full[s]);
-            bulk_load(zz, z0 + grow * (N / 8) + n0 / 8, zbytes, &full[s]);
-          }
+          tma_load_2d(w, wmap0, &full[s], n0 / 8, kb * kBK);
+          if (MODE == LR_FFN_MODE_SWIGLU) tma_load_2d(w + 512, wmap1, &full[s], n0 / 8, kb * kBK);
         }
       }
       if (ok) {
@@ -361,6 +351,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t idesc = umma_idesc_f16(128, BN, 1, 0);
       int it = 0, lt = 0;
       bool ok = true;
+      // Readiness of k-step `it` observed ahead of time: the barriers of the
+      // next k-step are tested (non-blocking) before this k-step's MMAs are
+      // issued, so the test latency overlaps the MMA issue instead of adding
+      // to it; a blocking wait is needed only when the test came back false.
+      bool pre_full = false, pre_dfull = false;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
         const int acc = lt & 1;
         const uint32_t aph = (lt >> 1) & 1;
@@ -375,11 +370,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t ph = (it / STAGES) & 1;
           const int q = it % kDStages;
           const uint32_t qph = (it / kDStages) & 1;
-          if (!wait_any(&full[s], ph, s_abort, err) || !wait_any(&dfull[q], qph, s_abort, err)) {
+          if ((!pre_full && !wait_any(&full[s], ph, s_abort, err)) ||
+              (!pre_dfull && !wait_any(&dfull[q], qph, s_abort, err))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const int it2 = it + 1;  // next k-step of this CTA's stream (maybe the next tile's)
+          const bool more = kb + 1 < KB || tile + int(gridDim.x) < total;
+          const bool nf = more && mbar_test_wait(&full[it2 % STAGES], (it2 / STAGES) & 1);
+          const bool nd = more && mbar_test_wait(&dfull[it2 % kDStages], (it2 / kDStages) & 1);
           const uint32_t aaddr = smem_u32(sA + q * kABytes);
           const uint32_t baddr = smem_u32(sB + s * L::kBStage);
 #pragma unroll
@@ -390,6 +390,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           umma_commit(&empty[s]);
           umma_commit(&dempty[q]);
+          pre_full = nf;
+          pre_dfull = nd;
         }
         if (!ok) break;
         umma_commit(&tfull[acc]);
@@ -401,37 +403,73 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp >= kEpiWarps) {
     // ------------------------------------------------------------ dequant
-    const int dtid = threadIdx.x - kEpiWarps * 32;  // 0..255
-    const int j = dtid & 15;                         // packed word column
-    const int rbase = dtid >> 4;                     // 0..15
+    // The dequant warps form kDStages groups of kWg warps; group g converts
+    // the k-steps it with it % kDStages == g into operand buffer g, so that
+    // kDStages k-steps (each a dependent load -> convert -> store -> fence
+    // chain) are in flight at once.
+    constexpr int kWg = kDeqWarps / kDStages;     // warps per group
+    constexpr int kGT = 32 * kWg;                 // threads per group
+    constexpr int kWords = 1024 / kGT;            // packed words per thread per k-step
+    constexpr int kRowStep = kGT / 16;            // rows between a thread's words
+    const int dtid = threadIdx.x - kEpiWarps * 32;
+    const int dgrp = dtid / kGT;
+    const int gt = dtid % kGT;
+    // j: packed word column of the 128-feature tile (0..15); rows rbase + kRowStep*i.
+    // SwiGLU keeps each warp on one box (gate or up), so a warp's loads cover
+    // contiguous bytes instead of two same-bank pieces.
+    int j, rbase, wbase, wstride;
+    if (MODE == LR_FFN_MODE_SWIGLU) {
+      const int half = gt / (kGT / 2), u = gt % (kGT / 2);
+      j = half * 8 + (u & 7);
+      rbase = u >> 3;
+      wbase = half * 512 + (u & 7);
+      wstride = 8;
+    } else {
+      j = gt & 15;
+      rbase = gt >> 4;
+      wbase = j;
+      wstride = 16;
+    }
     const int chunk = j & 7;
+    const int jm = (MODE == LR_FFN_MODE_SWIGLU) ? (j >> 3) : mat;  // matrix of this column
+    const int jw = (MODE == LR_FFN_MODE_SWIGLU) ? (j & 7) : j;      // word within the tile
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+      int e, mt, nt;
+      decode(tile, e, mt, nt);
+      const ExpertEntry* ent = table + e;
+      const int n0 = nt * BO;
+      const int g = ent->group_size;
+      // this thread's 8 features: scales row stride N, zeros row stride N/8
+      const bool jvalid = n0 + 8 * jw < N;
+      const __half* scol = ent->scales[jm] + n0 + 8 * jw;
+      const int32_t* zcol = ent->zeros[jm] + n0 / 8 + jw;
       for (int kb = 0; kb < KB; ++kb, ++it) {
+        if (it % kDStages != dgrp) continue;
+        const size_t grow = size_t((kb * kBK) / g);
+        uint4 sc = make_uint4(0, 0, 0, 0);
+        uint32_t zw = 0;
+        if (jvalid) {  // issued before the waits so their latency overlaps them
+          sc = __ldg(reinterpret_cast<const uint4*>(scol + grow * N));
+          zw = uint32_t(__ldg(zcol + grow * (N / 8)));
+        }
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        const int q = it % kDStages;
+        const int q = dgrp;
         const uint32_t qph = (it / kDStages) & 1;
         if (!wait_any(&full[s], ph, s_abort, err) || !wait_any(&dempty[q], qph ^ 1, s_abort, err)) {
           ok = false;
           break;
         }
         const uint32_t* w = sW + s * (kWBytes / 4);
-        const __half* ss = sS + s * (kSBytes / 2);
-        const uint32_t* zz = sZ + s * (kZBytes / 4);
         DeqParams P;
-        deq_params(zz[j], *reinterpret_cast<const uint4*>(ss + 8 * j), P);
+        deq_params(zw, sc, P);
         uint8_t* abuf = sA + q * kABytes + (j >> 3) * 8192;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = rbase + 16 * i;
-          uint32_t word;
-          if (MODE == LR_FFN_MODE_SWIGLU)
-            word = (j < 8) ? w[r * 8 + j] : w[512 + r * 8 + (j - 8)];
-          else
-            word = w[r * 16 + j];
-          const uint4 o = deq_word(word, P);
+        for (int i = 0; i < kWords; ++i) {
+          const int r = rbase + kRowStep * i;
+          const uint4 o = deq_word(w[wbase + r * wstride], P);
           *reinterpret_cast<uint4*>(abuf + (r >> 3) * 1024 + (r & 7) * 128 +
                                     ((chunk ^ (r & 7)) << 4)) = o;
         }
@@ -440,14 +478,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&dfull[q]);
       }
     }
-    // Dequant tail: the last operand buffers are released by asynchronous
-    // tcgen05.commit arrivals; wait for them before the CTA can exit.
+    // Dequant tail: the group's operand buffer is released by an asynchronous
+    // tcgen05.commit arrival; wait for the last one before the CTA can exit.
     for (int i = 0; ok && i < kDStages; ++i, ++it) {
-      if (!wait_any(&dempty[it % kDStages], ((it / kDStages) & 1) ^ 1, s_abort, err)) break;
+      if (it % kDStages != dgrp) continue;
+      if (!wait_any(&dempty[dgrp], ((it / kDStages) & 1) ^ 1, s_abort, err)) break;
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int etid = threadIdx.x;  // 0..127 == TMEM lane == feature in tile
+    // Two groups of four warps; warp w reads TMEM lanes 32*(w%4).. and group
+    // w/4 takes every other 16-column chunk, with its own named barrier and
+    // staging buffer.
+    const int grp = warp >> 2;
+    const int bar_id = 1 + grp;
+    const int etid = (warp & 3) * 32 + lane;    // 0..127 == TMEM lane
+    const int fe = lane_feature(etid);          // feature of this lane within the tile
+    const int fe64 = lane_feature(etid & 63);   // SwiGLU: gate/up feature of this lane
+    uint8_t* sCg = sC + grp * kCBytes;
     int lt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
@@ -455,11 +502,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       decode(tile, e, mt, nt);
       const int acc = lt & 1;
       const uint32_t aph = (lt >> 1) & 1;
-      // the four epilogue warps leave together: a failed wait is published
-      // before the named barrier and read by all after it
-      if (!wait_any(&tfull[acc], aph, s_abort, err)) *s_epi_fail = 1;
-      named_bar_epi();
-      if (*s_epi_fail) {
+      // a group leaves together: the barrier reduces "any wait failed"
+      const bool waited = wait_any(&tfull[acc], aph, s_abort, err);
+      if (named_bar_any(bar_id, !waited)) {
         ok = false;
         break;
       }
@@ -467,56 +512,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row_base = s_start[e] + mt * BN;
       const int rows_valid = min(BN, s_len[e] - mt * BN);
       const int n0 = nt * BO;
-      const uint32_t tbase = tmem_base + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
-      for (int c = 0; c < BN / 16; ++c) {
+      const uint32_t tbase =
+          tmem_base + (uint32_t((warp & 3) * 32) << 16) + uint32_t(acc * BN);
+      for (int c = grp; c < BN / 16; c += 2) {
         if (c * 16 >= rows_valid) break;
         uint32_t v[16];
         tmem_ld_32x32b_x16_sync(tbase + c * 16, v);
         const int nrow = min(16, rows_valid - c * 16);
         if (MODE != LR_FFN_MODE_SWIGLU) {
-          __half* stage = reinterpret_cast<__half*>(sC);  // [16][128]
+          __half* stage = reinterpret_cast<__half*>(sCg);  // [16][128]
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
             float f = __uint_as_float(v[jj]);
             if (MODE == LR_FFN_MODE_SILU) f = silu_f32(f);
-            stage[jj * 128 + etid] = __float2half_rn(f);
+            stage[jj * 128 + fe] = __float2half_rn(f);
           }
-          named_bar_epi();
+          named_bar(bar_id);
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int idx = etid + i * 128;
             const int row = idx >> 4, ch = idx & 15;
             if (row < nrow && n0 + ch * 8 < N) {
               *reinterpret_cast<uint4*>(C + size_t(row_base + c * 16 + row) * N + n0 + ch * 8) =
-                  *reinterpret_cast<const uint4*>(sC + row * 256 + ch * 16);
+                  *reinterpret_cast<const uint4*>(sCg + row * 256 + ch * 16);
             }
           }
-          named_bar_epi();
+          named_bar(bar_id);
         } else {
-          float* sU = reinterpret_cast<float*>(sC);                // [16][64] fp32
-          __half* stage = reinterpret_cast<__half*>(sC + 4096);    // [16][64] fp16
+          float* sU = reinterpret_cast<float*>(sCg);                // [16][64] fp32
+          __half* stage = reinterpret_cast<__half*>(sCg + 4096);    // [16][64] fp16
           if (etid >= 64) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) sU[jj * 64 + (etid - 64)] = __uint_as_float(v[jj]);
+            for (int jj = 0; jj < 16; ++jj) sU[jj * 64 + fe64] = __uint_as_float(v[jj]);
           }
-          named_bar_epi();
+          named_bar(bar_id);
           if (etid < 64) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               const float gv = __uint_as_float(v[jj]);
-              const float uv = sU[jj * 64 + etid];
-              stage[jj * 64 + etid] = __float2half_rn(silu_f32(gv) * uv);
+              const float uv = sU[jj * 64 + fe64];
+              stage[jj * 64 + fe64] = __float2half_rn(silu_f32(gv) * uv);
             }
           }
-          named_bar_epi();
+          named_bar(bar_id);
           {
             const int row = etid >> 3, ch = etid & 7;
             if (row < nrow) {
               *reinterpret_cast<uint4*>(C + size_t(row_base + c * 16 + row) * N + n0 + ch * 8) =
-                  *reinterpret_cast<const uint4*>(sC + 4096 + row * 128 + ch * 16);
+                  *reinterpret_cast<const uint4*>(sCg + 4096 + row * 128 + ch * 16);
             }
           }
-          named_bar_epi();
+          named_bar(bar_id);
         }
       }
       tc_fence_before();
@@ -566,8 +612,10 @@ static int launch_gemm(const CUtensorMap& tmap_a, const ExpertEntry* table, int 
                        int N, const int32_t* seg_start, const int32_t* seg_len, int max_rows, int R,
                        __half* C, int32_t* err, cudaStream_t stream) {
   constexpr int STAGES = GemmStages<BN>::v;
-  using L = GemmLayout<BN, STAGES>;
-  auto kern = w4a16_grouped_gemm_kernel<BN, STAGES, MODE>;
+  constexpr int DSTAGES = GemmStages<BN>::d;
+  using L = GemmLayout<BN, STAGES, DSTAGES>;
+  static_assert(L::kTotal <= 227 * 1024, "shared memory budget");
+  auto kern = w4a16_grouped_gemm_kernel<BN, STAGES, DSTAGES, MODE>;
   static int configured = 0;
   if (!configured) {
     LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
