@@ -15,7 +15,11 @@ the single-GPU output.  Here the experts are sharded and tokens move:
 * kept rows are permuted into a compact send buffer grouped by owner rank
   (kernel phase 2), exchanged with ``all_to_all_single``, run through the
   local grouped W4A16 FFN, sent back with ``all_to_all_single`` and combined in
-  token order by the same combine kernel as on one GPU.
+  token order by the same combine kernel as on one GPU;
+* each rank's tokens are split into ``microbatches`` contiguous micro-batches
+  whose exchanges are issued asynchronously, so one micro-batch's all-to-all
+  overlaps another's expert GEMMs (capacity still follows the global slot order
+  over all ranks and micro-batches).
 
 Every kept row goes through the same per-row arithmetic as on one GPU, so the
 output equals the single-GPU output bit for bit.  The exchange needs the split
@@ -60,49 +64,66 @@ class ExchangePlan:
         return int(sum(self.recv_rows))
 
 
-def plan_exchange(stats: np.ndarray, rank: int, world: int, num_experts: int, top_k: int,
-                  capacity_factor: float, load_balance_weight: float) -> ExchangePlan:
-    """Host plan from the all-gathered ``stats`` (G, 1 + 2E) float64 rows of
-    ``[T_r, count_r[0..E), prob_sum_r[0..E)]``."""
+def plan_exchanges(stats: np.ndarray, rank: int, world: int, num_experts: int, top_k: int,
+                   capacity_factor: float, load_balance_weight: float,
+                   nchunks: int = 1) -> list:
+    """Host plans for this rank's ``nchunks`` exchanges from the all-gathered ``stats``.
+
+    ``stats`` has ``world * nchunks`` float64 rows ``[T, count[0..E), prob_sum[0..E)]``,
+    one per token shard, in global token order: rank-major, then micro-batch
+    (each rank's tokens may be split into ``nchunks`` contiguous micro-batches).
+    Plan ``c`` covers the exchange of micro-batch ``c``: every rank sends its
+    micro-batch-``c`` rows and receives the same micro-batch's rows of its
+    experts.  Capacity follows the global slot order over all shards.
+    """
     G, E = world, num_experts
     if E % G:
         raise ValueError(f"num_experts {E} must be divisible by the world size {G}")
     El = E // G
-    T_r = stats[:, 0].astype(np.int64)
     counts = np.rint(stats[:, 1:1 + E]).astype(np.int64)
-    psum = stats[:, 1 + E:1 + 2 * E]
-    T = int(T_r.sum())
+    T = int(stats[:, 0].sum())
     S = T * top_k
     C = expert_capacity(S, E, capacity_factor)
-    base = np.zeros_like(counts)
-    base[1:] = np.cumsum(counts, axis=0)[:-1]
-    kept = np.clip(C - base, 0, counts)
-    koff = np.zeros(E + 1, np.int64)
-    koff[1:] = np.cumsum(kept[rank])
-    send_rows = [int(kept[rank, q * El:(q + 1) * El].sum()) for q in range(G)]
-    mine = slice(rank * El, (rank + 1) * El)
-    recv_rows = [int(kept[q, mine].sum()) for q in range(G)]
-    # receive layout: [source rank][local expert]; GEMM layout: [local expert][source rank]
-    recv_off = np.zeros(G + 1, np.int64)
-    recv_off[1:] = np.cumsum(recv_rows)
-    tot = kept[:, mine].sum(axis=0)
-    seg_len = tot.astype(np.int32)
-    seg_start = np.zeros(El, np.int32)
-    seg_start[1:] = np.cumsum(tot)[:-1]
-    reorder = None
-    if El > 1:
-        idx = []
-        for el in range(El):
-            for q in range(G):
-                within = int(kept[q, rank * El:rank * El + el].sum())
-                st = int(recv_off[q]) + within
-                idx.append(np.arange(st, st + int(kept[q, rank * El + el]), dtype=np.int64))
-        reorder = np.concatenate(idx) if idx else np.zeros(0, np.int64)
+    base = np.cumsum(counts, axis=0) - counts         # exclusive, over shards in order
+    kept_all = np.clip(C - base, 0, counts)           # (G*nchunks, E)
     f = counts.sum(axis=0) / float(max(S, 1))
-    P = psum.sum(axis=0) / float(max(T, 1))
+    P = stats[:, 1 + E:1 + 2 * E].sum(axis=0) / float(max(T, 1))
     aux = float(load_balance_weight * E * float((f * P).sum()))
-    return ExchangePlan(T, C, base[rank].astype(np.int32), kept, koff.astype(np.int32),
-                        send_rows, recv_rows, reorder, seg_start, seg_len, aux)
+    # per destination rank / per local expert sums, shaped (G*nchunks, G, El)
+    per_dst = kept_all.reshape(G * nchunks, G, El)
+    send_tot = per_dst.sum(axis=2)                    # (G*nchunks, G) rows to each rank
+    mine = per_dst[:, rank, :]                        # (G*nchunks, El) rows for my experts
+    plans = []
+    for c in range(nchunks):
+        me = rank * nchunks + c
+        kept = kept_all[c::nchunks]                   # (G, E)
+        koff = np.zeros(E + 1, np.int32)
+        koff[1:] = np.cumsum(kept_all[me])
+        recv_m = mine[c::nchunks]                     # (G, El) from each source rank
+        recv_rows = recv_m.sum(axis=1).tolist()
+        tot = recv_m.sum(axis=0)
+        seg_start = np.zeros(El, np.int32)
+        seg_start[1:] = np.cumsum(tot)[:-1]
+        reorder = None
+        if El > 1:
+            # receive layout [source rank][local expert] -> GEMM layout [local expert][rank]
+            flat = recv_m.reshape(-1)
+            starts = (np.cumsum(flat) - flat).reshape(G, El).T.reshape(-1)
+            lens = recv_m.T.reshape(-1)
+            dst0 = np.cumsum(lens) - lens
+            reorder = (np.repeat(starts - dst0, lens) + np.arange(int(lens.sum()))).astype(np.int64)
+        plans.append(ExchangePlan(T, C, base[me].astype(np.int32), kept, koff,
+                                  send_tot[me].tolist(), recv_rows, reorder, seg_start,
+                                  tot.astype(np.int32), aux))
+    return plans
+
+
+def plan_exchange(stats: np.ndarray, rank: int, world: int, num_experts: int, top_k: int,
+                  capacity_factor: float, load_balance_weight: float, chunk: int = 0,
+                  nchunks: int = 1) -> ExchangePlan:
+    """The plan of one micro-batch; see :func:`plan_exchanges`."""
+    return plan_exchanges(stats, rank, world, num_experts, top_k, capacity_factor,
+                          load_balance_weight, nchunks)[chunk]
 
 
 class ExpertParallelMoE:
@@ -114,7 +135,7 @@ class ExpertParallelMoE:
     routing (aux is the global load-balancing loss).
     """
 
-    def __init__(self, layer, world: int, rank: int, group=None):
+    def __init__(self, layer, world: int, rank: int, group=None, microbatches: int = 1):
         if layer.num_experts % world:
             raise ValueError("num_experts must be divisible by the world size")
         self.layer = layer
@@ -126,12 +147,31 @@ class ExpertParallelMoE:
         self.k = layer.top_k
         self.cf = layer.moe_cfg.expert_capacity_factor
         self.lbw = layer.gate.load_balance_weight
+        self.microbatches = max(1, int(microbatches))
         self.stage_events: list | None = None
         self._last_recv = 0
+        self._pinned: torch.Tensor | None = None  # reused host staging for per-step metadata
+
+    def _to_device(self, arr: np.ndarray, dev, dtype) -> torch.Tensor:
+        """Copy a small host array to the device through a persistent pinned buffer."""
+        t = torch.from_numpy(np.ascontiguousarray(arr)).to(dtype)
+        nbytes = t.numel() * t.element_size()
+        if self._pinned is None or self._pinned.numel() < nbytes:
+            self._pinned = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8).pin_memory()
+        # the previous step's copy out of the staging buffer must be finished
+        if getattr(self, "_staging_event", None) is not None:
+            self._staging_event.synchronize()
+        stage = self._pinned[:nbytes].view(dtype)
+        stage.copy_(t.view(-1))
+        out = stage.to(dev, non_blocking=True)
+        self._staging_event = torch.cuda.Event()
+        self._staging_event.record()
+        return out
 
     @classmethod
-    def from_layer(cls, layer, world: int, rank: int, group=None) -> "ExpertParallelMoE":
-        return cls(layer, world, rank, group)
+    def from_layer(cls, layer, world: int, rank: int, group=None,
+                   microbatches: int = 1) -> "ExpertParallelMoE":
+        return cls(layer, world, rank, group, microbatches)
 
     def _mark(self, name):
         if self.stage_events is not None:
@@ -148,51 +188,85 @@ class ExpertParallelMoE:
         dev = x.device
         x = x.reshape(-1, x.shape[-1]).to(torch.float16).contiguous()
         T_l, d = x.shape
-        E, G = self.E, self.world
+        E, G, El = self.E, self.world, self.El
+        nc = self.microbatches if T_l >= 256 * self.microbatches else 1
+        bounds = [T_l * c // nc for c in range(nc + 1)]
         err = _ext.error_word(dev.index)
         self._mark("begin")
         logits = self.layer.gate.logits(x)
         self._mark("gate")
-        ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = ops.topk_route(
-            logits, self.k, 1, float(self.lbw), err)
-        stats_l = torch.cat([torch.full((1,), float(T_l), dtype=torch.float64, device=dev),
-                             (offs[1:] - offs[:-1]).double(), psum])
-        stats = torch.empty(G * (1 + 2 * E), dtype=torch.float64, device=dev)
+        # phase 1 for every micro-batch, then one gather of all shard statistics
+        routes, stats_l = [], []
+        for c in range(nc):
+            lo, hi = bounds[c], bounds[c + 1]
+            r = ops.topk_route(logits[lo:hi], self.k, 1, float(self.lbw), err)
+            ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = r
+            routes.append((ids, gw, pos, ws))
+            stats_l.append(torch.cat([torch.full((1,), float(hi - lo), dtype=torch.float64,
+                                                 device=dev),
+                                      (offs[1:] - offs[:-1]).double(), psum]))
+        stats_l = torch.cat(stats_l)
+        stats = torch.empty(G * stats_l.numel(), dtype=torch.float64, device=dev)
         dist.all_gather_into_tensor(stats, stats_l, group=self.group)
-        plan = plan_exchange(stats.view(G, -1).cpu().numpy(), self.rank, G, E, self.k, self.cf,
-                             self.lbw)
-        meta_h = np.concatenate([plan.rank_base, plan.koff, plan.seg_start, plan.seg_len])
-        meta = torch.from_numpy(meta_h.astype(np.int32)).pin_memory().to(dev, non_blocking=True)
-        rank_base = meta[:E]
-        koff = meta[E:2 * E + 1]
-        seg_start = meta[2 * E + 1:2 * E + 1 + self.El]
-        seg_len = meta[2 * E + 1 + self.El:]
-        n_send, n_recv = plan.n_send, plan.n_recv
-        send, _rw, _src = ops.permute_tokens(x, ids, gw, koff, rank_base, plan.capacity, True,
-                                             False, pos, ws, n_send, E)
+        stats_h = stats.view(G * nc, -1).cpu().numpy()  # the one host synchronisation
+        plans = plan_exchanges(stats_h, self.rank, G, E, self.k, self.cf, self.lbw, nc)
+        # phase 2 + dispatch exchange for every micro-batch (asynchronous collectives)
+        sends, recvs, metas, dwork = [], [], [], []
+        for c, plan in enumerate(plans):
+            ids, gw, pos, ws = routes[c]
+            idx_h = plan.reorder if (plan.reorder is not None and plan.n_recv) else \
+                np.zeros(0, np.int64)
+            meta = self._to_device(np.concatenate([plan.rank_base, plan.koff, plan.seg_start,
+                                                   plan.seg_len, idx_h]).astype(np.int32),
+                                   dev, torch.int32)
+            metas.append(meta)
+            xs = x[bounds[c]:bounds[c + 1]]
+            send, _rw, _src = ops.permute_tokens(xs, ids, gw, meta[E:2 * E + 1], meta[:E],
+                                                 plan.capacity, True, False, pos, ws,
+                                                 plan.n_send, E)
+            recv = torch.empty(max(plan.n_recv, 1), d, dtype=torch.float16, device=dev)
+            sends.append(send)
+            recvs.append(recv)
+            dwork.append(dist.all_to_all_single(recv[:plan.n_recv], send[:plan.n_send],
+                                                plan.recv_rows, plan.send_rows,
+                                                group=self.group, async_op=True))
         self._mark("dispatch")
-        recv = torch.empty(max(n_recv, 1), d, dtype=torch.float16, device=dev)
-        dist.all_to_all_single(recv[:n_recv], send[:n_send], plan.recv_rows, plan.send_rows,
-                               group=self.group)
-        self._mark("a2a_dispatch")
-        if plan.reorder is not None and n_recv:
-            idx = torch.from_numpy(plan.reorder).pin_memory().to(dev, non_blocking=True)
-            a = recv[:n_recv].index_select(0, idx)
-        else:
-            idx, a = None, recv[:max(n_recv, 1)]
-        y = self.layer.experts.forward_segments(a, seg_start, seg_len, plan.capacity,
-                                                first_expert=self.rank * self.El,
-                                                num_local=self.El, mark=self._mark)
-        if idx is not None:
-            y_send = torch.empty_like(y)
-            y_send.index_copy_(0, idx, y)
-        else:
-            y_send = y
-        back = torch.empty(max(n_send, 1), d, dtype=torch.float16, device=dev)
-        dist.all_to_all_single(back[:n_send], y_send[:n_recv], plan.send_rows, plan.recv_rows,
-                               group=self.group)
-        self._mark("a2a_combine")
-        out = combine(back, gw, pos, T_l, self.k)
+        # expert FFN per micro-batch as soon as its rows arrived; combine exchange async
+        backs, cwork = [], []
+        for c, plan in enumerate(plans):
+            dwork[c].wait()
+            if c == 0:
+                self._mark("a2a_dispatch")
+            meta = metas[c]
+            seg_start = meta[2 * E + 1:2 * E + 1 + El]
+            seg_len = meta[2 * E + 1 + El:2 * E + 1 + 2 * El]
+            n_recv, n_send = plan.n_recv, plan.n_send
+            if plan.reorder is not None and n_recv:
+                idx = meta[2 * E + 1 + 2 * El:].long()
+                a = recvs[c][:n_recv].index_select(0, idx)
+            else:
+                idx, a = None, recvs[c]
+            y = self.layer.experts.forward_segments(
+                a, seg_start, seg_len, plan.capacity, first_expert=self.rank * El,
+                num_local=El, mark=self._mark if c == nc - 1 else None)
+            if idx is not None:
+                y_send = torch.empty_like(y)
+                y_send.index_copy_(0, idx, y)
+            else:
+                y_send = y
+            back = torch.empty(max(n_send, 1), d, dtype=torch.float16, device=dev)
+            backs.append(back)
+            cwork.append(dist.all_to_all_single(back[:n_send], y_send[:n_recv], plan.send_rows,
+                                                plan.recv_rows, group=self.group,
+                                                async_op=True))
+        outs = []
+        for c in range(nc):
+            cwork[c].wait()
+            if c == 0:
+                self._mark("a2a_combine")
+            _ids, gw, pos, _ws = routes[c]
+            outs.append(combine(backs[c], gw, pos, bounds[c + 1] - bounds[c], self.k))
+        out = outs[0] if nc == 1 else torch.cat(outs)
         self._mark("combine")
-        self._last_recv = n_recv
-        return out, torch.tensor(plan.aux_loss, dtype=torch.float32, device=dev)
+        self._last_recv = sum(p.n_recv for p in plans)
+        return out, torch.tensor(plans[0].aux_loss, dtype=torch.float32, device=dev)

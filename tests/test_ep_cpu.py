@@ -166,3 +166,43 @@ def test_dead_rank_is_detected_by_timeout():
         if p.is_alive():
             p.kill()
     assert status == "error", (status, info)
+
+
+@pytest.mark.parametrize("world,nchunks,E,k,cf", [(2, 2, 4, 2, 1.0), (4, 2, 8, 2, 0.8),
+                                                  (8, 2, 64, 6, 1.5), (2, 3, 8, 3, 1.25)])
+def test_microbatch_plans_follow_global_slot_order(world, nchunks, E, k, cf):
+    """Kept slots of every (rank, micro-batch) shard equal the single-process capacity rule,
+    and the exchange sizes agree between senders and receivers."""
+    from lightning_router.serving.ep import plan_exchanges
+    rng = np.random.default_rng(world * 100 + E)
+    Ts = rng.integers(5, 60, size=world * nchunks)
+    logits = [rng.standard_normal((int(t), E)).astype(np.float32) + np.linspace(1, -1, E)
+              for t in Ts]
+    ids = [orc.topk_gating(l, k)[0].reshape(-1) for l in logits]
+    stats = np.stack([np.concatenate([[ids_i.size // k], np.bincount(ids_i, minlength=E),
+                                      np.zeros(E)]) for ids_i in ids]).astype(np.float64)
+    plans = [plan_exchanges(stats, r, world, E, k, cf, 0.01, nchunks) for r in range(world)]
+    all_ids = np.concatenate(ids)
+    C = orc.capacity(all_ids.size, E, cf)
+    r_ref = orc.dispatch(all_ids, np.ones(all_ids.size, np.float32),
+                         np.zeros(all_ids.size, np.int32), E, C)
+    got, El = [], E // world
+    for r in range(world):
+        for c in range(nchunks):
+            p = plans[r][c]
+            assert p.capacity == C
+            loc = ids[r * nchunks + c]
+            order = np.argsort(loc, kind="stable")
+            cnt = np.bincount(loc, minlength=E)
+            lr = np.empty_like(loc)
+            lr[order] = np.arange(loc.size) - (np.cumsum(cnt) - cnt)[loc[order]]
+            kept = p.rank_base[loc] + lr < C
+            got.append(kept)
+            assert p.n_send == int(kept.sum())
+            # what rank r sends to q in micro-batch c is what q receives from r
+            for q in range(world):
+                assert plans[q][c].recv_rows[r] == p.send_rows[q]
+            if p.reorder is not None:
+                assert sorted(p.reorder.tolist()) == list(range(p.n_recv))
+            assert int(p.seg_len.sum()) == p.n_recv
+    np.testing.assert_array_equal(np.concatenate(got), r_ref.kept)
