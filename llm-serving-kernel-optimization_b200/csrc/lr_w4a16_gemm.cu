@@ -1,22 +1,32 @@
 // lr_w4a16_gemm.cu -- grouped W4A16 expert GEMM on tcgen05 (sm_100a).
 //
-// Swap-AB formulation: for expert e and a tile of BM = 128 weight columns
-// (output features) x BN tokens,
-//     D[feature, token] = sum_k W[k, feature] * A[token, k]
-// with W (dequantized INT4) as the UMMA "A" operand (M = 128, MN-major) and the
-// token rows as the UMMA "B" operand (N = BN, K-major).  The accumulator lives
-// in tensor memory (128 lanes = features, BN fp32 columns = tokens), double
-// buffered so the epilogue of one tile overlaps the main loop of the next.
+// Tile: token rows of one expert (the UMMA M operand, K-major, TMA loaded) x
+// WN dequantized weight columns (the UMMA N operand, MN-major, written by the
+// dequant warps).  For SwiGLU the WN columns are WN/2 gate and the same WN/2 up
+// features, so one accumulator row holds both halves of every output it needs.
+// Accumulators (TMEM lane = token row, one fp32 column per weight column) are
+// double buffered so the epilogue of one tile overlaps the main loop of the next.
+//
+// Two tile shapes share the kernel (MT = number of 128-row M sub-tiles):
+//   MT = 1, WN = 256: short expert segments (decode).  Each tcgen05.mma is
+//     issued by one thread at a roughly fixed cost, so 256 weight columns
+//     (2 KB of INT4 per 16-deep step) stand behind every instruction; only
+//     TOKROWS (32, 64 or 128) token rows are loaded per stage and the rest of
+//     the 128 M rows are left unused.
+//   MT = 2, WN = 128: long segments (prefill).  256 token rows share each
+//     dequantized weight column, halving the dequant work (the CUDA-core side
+//     of the pipeline) per tensor-core FLOP.
 //
 // Warp roles (576 threads, one CTA per SM, persistent over tiles):
-//   warps 0-7   epilogue (two groups of four, alternate 16-token chunks):
-//               tcgen05.ld -> activation -> fp16 -> staged in smem -> coalesced
-//               16-byte stores (rows clipped to the expert segment)
-//   warps 8-15  dequant: packed int32 words (TMA-staged) -> 8 fp16 each,
-//               fp16(scale * (q - zero)) computed exactly, written into the
-//               128-byte-swizzled MN-major operand buffer
-//   warp 16     producer: TMA tile loads of tokens and packed weights (the
-//               dequant warps read the per-group scales / zeros themselves)
+//   warps 0-7   epilogue, two groups of four (warp w reads TMEM lanes 32*(w%4)..);
+//               MT = 2: group g drains M sub-tile g; MT = 1: the groups take
+//               alternate 16-column chunks.  tcgen05.ld -> activation -> fp16 ->
+//               16-byte stores of the token row
+//   warps 8-15  dequant, in DGROUPS groups that take alternate k-steps: packed
+//               int32 words (TMA-staged) + per-group scale / zero (read from
+//               global memory) -> fp16(scale * (q - zero)), written into the
+//               128-byte-swizzled MN-major operand buffer of their k-step
+//   warp 16     producer: TMA loads of the token box and the packed weight box(es)
 //   warp 17     TMEM allocation + single-thread tcgen05.mma issue
 //
 // Every mbarrier wait is bounded in time; a wait that runs out raises a
@@ -32,8 +42,9 @@ namespace lr {
 // per-expert weight table (device resident, written once per weight set)
 // ---------------------------------------------------------------------------
 struct alignas(128) ExpertEntry {
-  CUtensorMap qw16[3];  // packed weights, box {16 words, 64 rows}
-  CUtensorMap qw8[3];   // packed weights, box {8 words, 64 rows}
+  CUtensorMap qw32[3];  // packed weights, box {32 words = 256 features, 64 rows}
+  CUtensorMap qw16[3];  // packed weights, box {16 words = 128 features, 64 rows}
+  CUtensorMap qw8[3];   // packed weights, box {8 words = 64 features, 64 rows}
   const __half* scales[3];
   const int32_t* zeros[3];
   int32_t K[3];
@@ -48,47 +59,45 @@ constexpr int kDeqWarps = 8;
 constexpr int kProdWarp = kEpiWarps + kDeqWarps;
 constexpr int kMmaWarp = kProdWarp + 1;
 constexpr int kGemmThreads = (kMmaWarp + 1) * 32;
-constexpr int kBK = 64;
+constexpr int kBK = 64;       // k per pipeline step
+constexpr int kAccCols = 256;  // TMEM columns per accumulator (MT * WN)
 constexpr int kMaxGemmExperts = 256;
-constexpr int kABytes = 128 * kBK * 2;      // dequantized operand, one buffer
-constexpr int kWBytes = kBK * 16 * 4;       // packed weights per stage (128 features)
-constexpr int kCBytes = 6144;               // epilogue staging: [16][128] fp16, or [16][64] fp32 + [16][64] fp16
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 constexpr uint64_t kDrainLimitNs = 100000000ull;  // 100 ms
 
-template <int BN, int STAGES, int DSTAGES>
-struct GemmLayout {
-  static constexpr int kDStages = DSTAGES;
-  static constexpr int kBStage = BN * 128;
-  static constexpr int offB = 0;
-  static constexpr int offA = offB + STAGES * kBStage;
-  static constexpr int offW = offA + kDStages * kABytes;
-  static constexpr int offC = offW + STAGES * kWBytes;
-  static constexpr int offBar = offC + 2 * kCBytes;
-  static constexpr int kNumBars = 2 * STAGES + 2 * kDStages + 4 + 1;
+// Tile shape: MT sub-tiles of 128 M rows (TOKROWS loaded per sub-tile) x WN
+// weight columns; STAGES TMA stages (tokens + packed weights), DSTAGES
+// dequantized-operand buffers and DGROUPS dequant warp groups.
+template <int TOKROWS_, int MT_, int STAGES_, int DSTAGES_, int DGROUPS_>
+struct GemmShape {
+  static constexpr int TOKROWS = TOKROWS_, MT = MT_, STAGES = STAGES_, DSTAGES = DSTAGES_,
+                       DGROUPS = DGROUPS_;
+  static constexpr int WN = kAccCols / MT;             // weight columns per tile (UMMA N)
+  static constexpr int WJ = WN / 8;                    // packed words per weight row
+  static constexpr int ROWS = MT * TOKROWS;            // token rows per tile
+  static constexpr int kAStage = ROWS * kBK * 2;       // token box bytes
+  static constexpr int kWStage = kBK * WN / 2;         // packed weight bytes per stage
+  static constexpr int kBBuf = WN * kBK * 2;           // dequantized operand buffer
+  static constexpr int offA = 0;
+  static constexpr int offB = offA + STAGES * kAStage;
+  static constexpr int offW = offB + DSTAGES * kBBuf;
+  static constexpr int offBar = offW + STAGES * kWStage;
+  static constexpr int kNumBars = 2 * STAGES + DSTAGES + 4 + 1;
   static constexpr int offMisc = offBar + kNumBars * 8;
-  static constexpr int kMiscInts = 8;
-  static constexpr int offTab = offMisc + kMiscInts * 4;
+  static constexpr int offTab = offMisc + 8 * 4;
   static constexpr int kTabBytes = (kMaxGemmExperts * 4 + 1) * 4;
   static constexpr int kTotal = offTab + kTabBytes + 1024;  // + base alignment slack
-  static_assert(offA % 1024 == 0, "operand alignment");
+  static_assert(offB % 1024 == 0 && offW % 1024 == 0, "operand alignment");
+  static_assert(MT == 1 || TOKROWS == 128, "stacked M sub-tiles are full");
+  static_assert(ROWS <= 256, "TMA box height");
+  static_assert(kDeqWarps % DGROUPS == 0 && DGROUPS <= DSTAGES, "dequant groups");
+  static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-// Pipeline depths per token tile: v = TMA stages (tokens + packed weights),
-// d = dequantized-operand buffers.  Small tiles do little tensor work per k-step,
-// so the dequant -> MMA -> release chain must be deeper to hide its latency.
-template <int BN>
-struct GemmStages;
-template <>
-struct GemmStages<16> { static constexpr int v = 16, d = 4; };
-template <>
-struct GemmStages<32> { static constexpr int v = 16, d = 4; };
-template <>
-struct GemmStages<64> { static constexpr int v = 10, d = 4; };
-template <>
-struct GemmStages<128> { static constexpr int v = 8, d = 2; };
-template <>
-struct GemmStages<256> { static constexpr int v = 4, d = 2; };
+using ShapeR32 = GemmShape<32, 1, 7, 4, 4>;
+using ShapeR64 = GemmShape<64, 1, 5, 4, 4>;
+using ShapeR128 = GemmShape<128, 1, 6, 2, 2>;
+using ShapeR256 = GemmShape<128, 2, 4, 4, 2>;
 
 // ---------------------------------------------------------------------------
 // int4 -> fp16 dequantization of one packed word (8 features)
@@ -133,8 +142,8 @@ LR_DEVICE void deq_params(uint32_t zword, uint4 sc, DeqParams& P) {
 // fp16(scale * (q - z)): (1024+q) - (1024+z) is exact in fp16, and the product
 // of an fp16 scale with an integer in [-15, 15] is rounded once.  The eight
 // halves come out in the order f0 f4 f1 f5 f2 f6 f3 f7; the operand keeps that
-// order (a permutation of the tile's M rows) and the epilogue maps each
-// accumulator lane back to its feature with lane_feature().
+// order (a permutation of the tile's N columns) and the epilogue puts each
+// group of eight accumulator columns back into feature order.
 LR_DEVICE uint4 deq_word(uint32_t w, const DeqParams& P) {
   uint4 o;
   o.x = h2_mul(h2_sub(nib_pair(w, 0), P.z[0]), P.s[0]);
@@ -144,13 +153,20 @@ LR_DEVICE uint4 deq_word(uint32_t w, const DeqParams& P) {
   return o;
 }
 
-// Feature (within its 8-feature group) held by accumulator lane `lane`.
-LR_DEVICE int lane_feature(int lane) { return (lane & ~7) | ((lane & 7) >> 1) | ((lane & 1) << 2); }
+// Eight accumulator columns in the operand's order (f0 f4 f1 f5 f2 f6 f3 f7)
+// -> eight fp16 features in order.
+LR_DEVICE uint4 pack8_feature_order(const float* v) {
+  uint4 o;
+  __half2* h = reinterpret_cast<__half2*>(&o);
+  h[0] = __floats2half2_rn(v[0], v[2]);  // f0 f1
+  h[1] = __floats2half2_rn(v[4], v[6]);  // f2 f3
+  h[2] = __floats2half2_rn(v[1], v[3]);  // f4 f5
+  h[3] = __floats2half2_rn(v[5], v[7]);  // f6 f7
+  return o;
+}
 
-// Named barrier over the 128 threads of one epilogue group.
-LR_DEVICE void named_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-
-// Named barrier that also returns whether any of the 128 threads passed `pred`.
+// Named barrier over the 128 threads of one epilogue group that also returns
+// whether any of them passed `pred`.
 LR_DEVICE bool named_bar_any(int id, bool pred) {
   uint32_t r;
   asm volatile(
@@ -179,33 +195,32 @@ LR_DEVICE void wait_drain(uint64_t* bar, uint32_t parity) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, int DSTAGES, int MODE>
+template <class S, int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4a16_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const ExpertEntry* __restrict__ table, int E, int mat, int K, int N,
                               const int32_t* __restrict__ seg_start,
                               const int32_t* __restrict__ seg_len, int max_rows, int R,
                               __half* __restrict__ C, int32_t* err) {
-  using L = GemmLayout<BN, STAGES, DSTAGES>;
-  constexpr int kDStages = DSTAGES;
-  constexpr int BO = (MODE == LR_FFN_MODE_SWIGLU) ? 64 : 128;  // output features per tile
+  constexpr int STAGES = S::STAGES, DSTAGES = S::DSTAGES, DGROUPS = S::DGROUPS;
+  constexpr int MT = S::MT, WN = S::WN, WJ = S::WJ, ROWS = S::ROWS;
+  constexpr bool kGLU = MODE == LR_FFN_MODE_SWIGLU;
+  constexpr int BO = kGLU ? WN / 2 : WN;  // output features per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sB = smem + L::offB;
-  uint8_t* sA = smem + L::offA;
-  uint32_t* sW = reinterpret_cast<uint32_t*>(smem + L::offW);
-  uint8_t* sC = smem + L::offC;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::offBar);
+  uint8_t* sA = smem + S::offA;
+  uint8_t* sB = smem + S::offB;
+  uint32_t* sW = reinterpret_cast<uint32_t*>(smem + S::offW);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);
   uint64_t* empty = full + STAGES;
   uint64_t* dfull = empty + STAGES;
-  uint64_t* dempty = dfull + kDStages;
-  uint64_t* tfull = dempty + kDStages;
+  uint64_t* tfull = dfull + DSTAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* fin = tempty + 2;
-  int* misc = reinterpret_cast<int*>(smem + L::offMisc);
+  int* misc = reinterpret_cast<int*>(smem + S::offMisc);
   volatile int* s_abort = misc;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 1);
-  int* s_tbase = reinterpret_cast<int*>(smem + L::offTab);  // E+1
+  int* s_tbase = reinterpret_cast<int*>(smem + S::offTab);  // E+1
   int* s_start = s_tbase + E + 1;                            // E
   int* s_len = s_start + E;                                  // E
   int* s_mt = s_len + E;                                     // E
@@ -219,10 +234,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < kDStages; ++i) {
-      mbar_init(&dfull[i], kDeqWarps / kDStages);
-      mbar_init(&dempty[i], 1);
-    }
+    for (int i = 0; i < DSTAGES; ++i) mbar_init(&dfull[i], kDeqWarps / DGROUPS);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], kEpiWarps * 32);
@@ -232,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(s_tmem, 2 * BN);
+    tmem_alloc(s_tmem, 2 * kAccCols);
     tmem_relinquish();
   }
   if (warp == kProdWarp) {
@@ -260,7 +272,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           len = 0;
         }
       }
-      const int mt = (len + BN - 1) / BN;
+      const int mt = (len + ROWS - 1) / ROWS;
       const int tiles = mt * n_tiles;
       int incl = tiles;
 #pragma unroll
@@ -284,6 +296,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *s_tmem;
   const int total = s_tbase[E];
 
+  // tile -> (expert, token tile, feature tile); token tiles vary fastest
   auto decode = [&](int tile, int& e, int& mt, int& nt) {
     int lo = 0, hi = E;  // last e with s_tbase[e] <= tile
     while (hi - lo > 1) {
@@ -306,17 +319,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int e, mt, nt;
         decode(tile, e, mt, nt);
         const ExpertEntry* ent = table + e;
-        const int row0 = s_start[e] + mt * BN;
+        const int row0 = s_start[e] + mt * ROWS;
         const int n0 = nt * BO;
-        const CUtensorMap* wmap0 = (MODE == LR_FFN_MODE_SWIGLU) ? &ent->qw8[0] : &ent->qw16[mat];
-        const CUtensorMap* wmap1 = &ent->qw8[1];
+        // PLAIN / SILU: one box of WJ words; SwiGLU: WJ/2 gate + WJ/2 up words
+        const CUtensorMap* wmap0;
+        if (kGLU) wmap0 = WN == 256 ? &ent->qw16[0] : &ent->qw8[0];
+        else wmap0 = WN == 256 ? &ent->qw32[mat] : &ent->qw16[mat];
+        const CUtensorMap* wmap1 = WN == 256 ? &ent->qw16[1] : &ent->qw8[1];
         // descriptors were written to global memory by a copy before the launch
         tensormap_acquire(wmap0);
-        if (MODE == LR_FFN_MODE_SWIGLU) tensormap_acquire(wmap1);
-        // Only the token box and the packed weight box(es) travel by TMA: each
-        // copy costs issue time on this single thread, so the small per-group
-        // scale / zero rows are read by the dequant warps themselves.
-        const uint32_t tx = uint32_t(BN * 128 + kWBytes);
+        if (kGLU) tensormap_acquire(wmap1);
+        // only the token box and the packed weight box(es) travel by TMA; the
+        // small per-group scale / zero rows are read by the dequant warps
+        const uint32_t tx = uint32_t(S::kAStage + S::kWStage);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -325,17 +340,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], tx);
-          tma_load_2d(sB + s * L::kBStage, &tmap_a, &full[s], kb * kBK, row0);
-          uint32_t* w = sW + s * (kWBytes / 4);
+          tma_load_2d(sA + s * S::kAStage, &tmap_a, &full[s], kb * kBK, row0);
+          uint32_t* w = sW + s * (S::kWStage / 4);
           tma_load_2d(w, wmap0, &full[s], n0 / 8, kb * kBK);
-          if (MODE == LR_FFN_MODE_SWIGLU) tma_load_2d(w + 512, wmap1, &full[s], n0 / 8, kb * kBK);
+          if (kGLU) tma_load_2d(w + S::kWStage / 8, wmap1, &full[s], n0 / 8, kb * kBK);
         }
       }
       if (ok) {
         // Producer tail: wait until the MMA has released every stage.  The
         // releases are tcgen05.commit arrivals that complete asynchronously;
         // leaving before they land would let them hit the barriers of the next
-        // CTA placed on this SM.
+        // CTA placed on this SM.  (The dequant buffers are released by the same
+        // arrivals.)
         for (int i = 0; i < STAGES; ++i, ++it) {
           if (!wait_any(&empty[it % STAGES], ((it / STAGES) & 1) ^ 1, s_abort, err)) break;
         }
@@ -348,13 +364,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(128, BN, 1, 0);
+      constexpr uint32_t idesc = umma_idesc_f16(128, WN, 0, 1);
       int it = 0, lt = 0;
       bool ok = true;
       // Readiness of k-step `it` observed ahead of time: the barriers of the
       // next k-step are tested (non-blocking) before this k-step's MMAs are
-      // issued, so the test latency overlaps the MMA issue instead of adding
-      // to it; a blocking wait is needed only when the test came back false.
+      // issued; a blocking wait is needed only when the test came back false.
       bool pre_full = false, pre_dfull = false;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
         const int acc = lt & 1;
@@ -364,12 +379,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * kAccCols);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          const int q = it % kDStages;
-          const uint32_t qph = (it / kDStages) & 1;
+          const int q = it % DSTAGES;
+          const uint32_t qph = (it / DSTAGES) & 1;
           if ((!pre_full && !wait_any(&full[s], ph, s_abort, err)) ||
               (!pre_dfull && !wait_any(&dfull[q], qph, s_abort, err))) {
             ok = false;
@@ -379,17 +394,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int it2 = it + 1;  // next k-step of this CTA's stream (maybe the next tile's)
           const bool more = kb + 1 < KB || tile + int(gridDim.x) < total;
           const bool nf = more && mbar_test_wait(&full[it2 % STAGES], (it2 / STAGES) & 1);
-          const bool nd = more && mbar_test_wait(&dfull[it2 % kDStages], (it2 / kDStages) & 1);
-          const uint32_t aaddr = smem_u32(sA + q * kABytes);
-          const uint32_t baddr = smem_u32(sB + s * L::kBStage);
+          const bool nd = more && mbar_test_wait(&dfull[it2 % DSTAGES], (it2 / DSTAGES) & 1);
+          const uint32_t aaddr = smem_u32(sA + s * S::kAStage);
+          const uint32_t baddr = smem_u32(sB + q * S::kBBuf);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t adesc = umma_smem_desc(aaddr + kk * 2048, 8192, 1024, 2);
-            const uint64_t bdesc = umma_smem_desc(baddr + kk * 32, 16, 1024, 2);
-            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            const uint64_t bdesc = umma_smem_desc(baddr + kk * 2048, 8192, 1024, 2);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              // M sub-tile m: token rows 128m.. (16 KB into the stage), TMEM columns WN*m..
+              const uint64_t adesc = umma_smem_desc(aaddr + m * 16384 + kk * 32, 16, 1024, 2);
+              umma_f16_ss(d_tmem + uint32_t(m * WN), adesc, bdesc, idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+            }
           }
+          // one release for both the token stage and the dequantized buffer
           umma_commit(&empty[s]);
-          umma_commit(&dempty[q]);
           pre_full = nf;
           pre_dfull = nd;
         }
@@ -403,39 +423,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp >= kEpiWarps) {
     // ------------------------------------------------------------ dequant
-    // The dequant warps form kDStages groups of kWg warps; group g converts
-    // the k-steps it with it % kDStages == g into operand buffer g, so that
-    // kDStages k-steps (each a dependent load -> convert -> store -> fence
-    // chain) are in flight at once.
-    constexpr int kWg = kDeqWarps / kDStages;     // warps per group
-    constexpr int kGT = 32 * kWg;                 // threads per group
-    constexpr int kWords = 1024 / kGT;            // packed words per thread per k-step
-    constexpr int kRowStep = kGT / 16;            // rows between a thread's words
+    // DGROUPS groups of kWg warps; group g converts the k-steps it with
+    // it % DGROUPS == g into operand buffer it % DSTAGES, so several k-steps
+    // (each a dependent load -> convert -> store -> fence chain) can be in
+    // flight at once.  A buffer is free again once the MMA of the k-step that
+    // used it before (it - DSTAGES) completed, i.e. once that k-step's stage was
+    // released.
+    constexpr int kWg = kDeqWarps / DGROUPS;          // warps per group
+    constexpr int kGT = 32 * kWg;                     // threads per group
+    constexpr int kWords = (S::kWStage / 4) / kGT;    // packed words per thread per k-step
+    constexpr int kRowStep = kGT / WJ;                // rows between a thread's words
+    static_assert(kWords * kRowStep == kBK, "dequant thread mapping");
     const int dtid = threadIdx.x - kEpiWarps * 32;
     const int dgrp = dtid / kGT;
     const int gt = dtid % kGT;
-    // j: packed word column of the 128-feature tile (0..15); rows rbase + kRowStep*i.
-    // SwiGLU keeps each warp on one box (gate or up), so a warp's loads cover
-    // contiguous bytes instead of two same-bank pieces.
+    // j: packed word column of the tile (0..WJ-1); rows rbase + kRowStep*i.
+    // SwiGLU: the gate box holds words 0..WJ/2-1 and the up box the rest; each
+    // warp stays on one box so its loads cover 128 contiguous bytes.
     int j, rbase, wbase, wstride;
-    if (MODE == LR_FFN_MODE_SWIGLU) {
+    if (kGLU) {
+      constexpr int WH = WJ / 2;
       const int half = gt / (kGT / 2), u = gt % (kGT / 2);
-      j = half * 8 + (u & 7);
-      rbase = u >> 3;
-      wbase = half * 512 + (u & 7);
-      wstride = 8;
+      j = half * WH + (u % WH);
+      rbase = u / WH;
+      wbase = half * (S::kWStage / 8) + (u % WH);
+      wstride = WH;
     } else {
-      j = gt & 15;
-      rbase = gt >> 4;
+      j = gt % WJ;
+      rbase = gt / WJ;
       wbase = j;
-      wstride = 16;
+      wstride = WJ;
     }
-    const int chunk = j & 7;
-    const int jm = (MODE == LR_FFN_MODE_SWIGLU) ? (j >> 3) : mat;  // matrix of this column
-    const int jw = (MODE == LR_FFN_MODE_SWIGLU) ? (j & 7) : j;      // word within the tile
-    int it = 0;
+    static_assert((kRowStep & (kRowStep - 1)) == 0, "row step is a power of two");
+    // Row r = rbase + kRowStep*i splits into a per-thread part and a constant
+    // part: r & 7 = (rbase & 7) | (kRowStep*i & 7) and r >> 3 = (rbase >> 3) +
+    // (kRowStep*i >> 3) (no carries, kRowStep a power of two and rbase <
+    // kRowStep or kRowStep a multiple of 8), so every store address is a
+    // per-thread base + an immediate + one xor of the swizzled chunk.
+    const int st_base = (j >> 3) * 8192 + (rbase >> 3) * 1024 + (rbase & 7) * 128;
+    const int cx = (j & 7) ^ (rbase & 7);
+    const int ld_base = wbase + rbase * wstride;
+    const int jm = kGLU ? (j / (WJ / 2)) : mat;   // matrix of this column
+    const int jw = kGLU ? (j % (WJ / 2)) : j;      // 8-feature word within the tile's slice
+    int it0 = 0;  // first k-step of the current tile in this CTA's stream
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+    for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, it0 += KB) {
       int e, mt, nt;
       decode(tile, e, mt, nt);
       const ExpertEntry* ent = table + e;
@@ -445,56 +477,77 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool jvalid = n0 + 8 * jw < N;
       const __half* scol = ent->scales[jm] + n0 + 8 * jw;
       const int32_t* zcol = ent->zeros[jm] + n0 / 8 + jw;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        if (it % kDStages != dgrp) continue;
+      auto load_params = [&](int kb, uint4& sc, uint32_t& zw) {
         const size_t grow = size_t((kb * kBK) / g);
-        uint4 sc = make_uint4(0, 0, 0, 0);
-        uint32_t zw = 0;
-        if (jvalid) {  // issued before the waits so their latency overlaps them
+        sc = make_uint4(0, 0, 0, 0);
+        zw = 0;
+        if (jvalid) {
           sc = __ldg(reinterpret_cast<const uint4*>(scol + grow * N));
           zw = uint32_t(__ldg(zcol + grow * (N / 8)));
         }
+      };
+      // this group's k-steps of the tile: kb = kb0, kb0 + DGROUPS, ...; the
+      // scale / zero row of the next one is requested before the current one
+      // is converted, so its latency hides behind a whole k-step
+      int kb = DGROUPS > 1 ? (dgrp - it0 % DGROUPS + DGROUPS) % DGROUPS : 0;
+      uint4 sc;
+      uint32_t zw;
+      if (kb < KB) load_params(kb, sc, zw);
+      for (; kb < KB; kb += DGROUPS) {
+        const int it = it0 + kb;
+        uint4 sc_next = sc;
+        uint32_t zw_next = zw;
+        if (kb + DGROUPS < KB) load_params(kb + DGROUPS, sc_next, zw_next);
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        const int q = dgrp;
-        const uint32_t qph = (it / kDStages) & 1;
-        if (!wait_any(&full[s], ph, s_abort, err) || !wait_any(&dempty[q], qph ^ 1, s_abort, err)) {
+        const int q = it % DSTAGES;
+        const int prev = it - DSTAGES;  // last k-step that used buffer q
+        if (!wait_any(&full[s], ph, s_abort, err) ||
+            (prev >= 0 &&
+             !wait_any(&empty[prev % STAGES], (prev / STAGES) & 1, s_abort, err))) {
           ok = false;
           break;
         }
-        const uint32_t* w = sW + s * (kWBytes / 4);
+        const uint32_t* w = sW + s * (S::kWStage / 4);
         DeqParams P;
         deq_params(zw, sc, P);
-        uint8_t* abuf = sA + q * kABytes + (j >> 3) * 8192;
+        uint8_t* bbuf = sB + q * S::kBBuf + st_base;
+        const uint32_t* wrow = w + ld_base;
+        // The packed words of a batch are all read before the first store: the
+        // compiler cannot move a shared-memory load above a store it may alias,
+        // and a load -> convert -> store chain per word would serialise on the
+        // load latency.
+        constexpr int kBatch = kWords < 8 ? kWords : 8;
 #pragma unroll
-        for (int i = 0; i < kWords; ++i) {
-          const int r = rbase + kRowStep * i;
-          const uint4 o = deq_word(w[wbase + r * wstride], P);
-          *reinterpret_cast<uint4*>(abuf + (r >> 3) * 1024 + (r & 7) * 128 +
-                                    ((chunk ^ (r & 7)) << 4)) = o;
+        for (int i0 = 0; i0 < kWords; i0 += kBatch) {
+          uint32_t wv[kBatch];
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) wv[i] = wrow[kRowStep * (i0 + i) * wstride];
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            const int rk = kRowStep * (i0 + i);  // constant part of the row
+            const uint4 o = deq_word(wv[i], P);
+            *reinterpret_cast<uint4*>(bbuf + (rk >> 3) * 1024 + (rk & 7) * 128 +
+                                      ((cx ^ (rk & 7)) << 4)) = o;
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dfull[q]);
+        sc = sc_next;
+        zw = zw_next;
       }
-    }
-    // Dequant tail: the group's operand buffer is released by an asynchronous
-    // tcgen05.commit arrival; wait for the last one before the CTA can exit.
-    for (int i = 0; ok && i < kDStages; ++i, ++it) {
-      if (it % kDStages != dgrp) continue;
-      if (!wait_any(&dempty[dgrp], ((it / kDStages) & 1) ^ 1, s_abort, err)) break;
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Two groups of four warps; warp w reads TMEM lanes 32*(w%4).. and group
-    // w/4 takes every other 16-column chunk, with its own named barrier and
-    // staging buffer.
     const int grp = warp >> 2;
-    const int bar_id = 1 + grp;
-    const int etid = (warp & 3) * 32 + lane;    // 0..127 == TMEM lane
-    const int fe = lane_feature(etid);          // feature of this lane within the tile
-    const int fe64 = lane_feature(etid & 63);   // SwiGLU: gate/up feature of this lane
-    uint8_t* sCg = sC + grp * kCBytes;
+    const int quarter = warp & 3;
+    // MT = 2: group g drains sub-tile g (all chunks); MT = 1: alternate chunks
+    const int msub = MT == 2 ? grp : 0;
+    const int c0 = MT == 2 ? 0 : grp;
+    constexpr int cstep = MT == 2 ? 1 : 2;
+    const int trow = msub * 128 + quarter * 32 + lane;  // token row within the tile
+    const bool warp_rows = quarter * 32 < S::TOKROWS;
     int lt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
@@ -504,65 +557,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t aph = (lt >> 1) & 1;
       // a group leaves together: the barrier reduces "any wait failed"
       const bool waited = wait_any(&tfull[acc], aph, s_abort, err);
-      if (named_bar_any(bar_id, !waited)) {
+      if (named_bar_any(1 + grp, !waited)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int row_base = s_start[e] + mt * BN;
-      const int rows_valid = min(BN, s_len[e] - mt * BN);
+      const int rows_valid = min(ROWS, s_len[e] - mt * ROWS);
+      const bool row_ok = trow < rows_valid;
+      __half* crow = C + size_t(s_start[e] + mt * ROWS + (row_ok ? trow : 0)) * N;
       const int n0 = nt * BO;
-      const uint32_t tbase =
-          tmem_base + (uint32_t((warp & 3) * 32) << 16) + uint32_t(acc * BN);
-      for (int c = grp; c < BN / 16; c += 2) {
-        if (c * 16 >= rows_valid) break;
-        uint32_t v[16];
-        tmem_ld_32x32b_x16_sync(tbase + c * 16, v);
-        const int nrow = min(16, rows_valid - c * 16);
-        if (MODE != LR_FFN_MODE_SWIGLU) {
-          __half* stage = reinterpret_cast<__half*>(sCg);  // [16][128]
+      const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) +
+                             uint32_t(acc * kAccCols + msub * WN);
+      if (warp_rows && msub * 128 + quarter * 32 < rows_valid) {
+        for (int c = c0; c < BO / 16; c += cstep) {
+          const int f0 = n0 + c * 16;
+          if (f0 >= N) break;
+          uint32_t v[16];
+          float f[16];
+          tmem_ld_32x32b_x16_sync(tbase + c * 16, v);
+          if (kGLU) {
+            uint32_t u[16];
+            tmem_ld_32x32b_x16_sync(tbase + WN / 2 + c * 16, u);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            float f = __uint_as_float(v[jj]);
-            if (MODE == LR_FFN_MODE_SILU) f = silu_f32(f);
-            stage[jj * 128 + fe] = __float2half_rn(f);
-          }
-          named_bar(bar_id);
+            for (int i = 0; i < 16; ++i)
+              f[i] = silu_f32(__uint_as_float(v[i])) * __uint_as_float(u[i]);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int idx = etid + i * 128;
-            const int row = idx >> 4, ch = idx & 15;
-            if (row < nrow && n0 + ch * 8 < N) {
-              *reinterpret_cast<uint4*>(C + size_t(row_base + c * 16 + row) * N + n0 + ch * 8) =
-                  *reinterpret_cast<const uint4*>(sCg + row * 256 + ch * 16);
+            for (int i = 0; i < 16; ++i) {
+              f[i] = __uint_as_float(v[i]);
+              if (MODE == LR_FFN_MODE_SILU) f[i] = silu_f32(f[i]);
             }
           }
-          named_bar(bar_id);
-        } else {
-          float* sU = reinterpret_cast<float*>(sCg);                // [16][64] fp32
-          __half* stage = reinterpret_cast<__half*>(sCg + 4096);    // [16][64] fp16
-          if (etid >= 64) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) sU[jj * 64 + fe64] = __uint_as_float(v[jj]);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + f0);
+            dst[0] = pack8_feature_order(f);
+            dst[1] = pack8_feature_order(f + 8);
           }
-          named_bar(bar_id);
-          if (etid < 64) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const float gv = __uint_as_float(v[jj]);
-              const float uv = sU[jj * 64 + fe64];
-              stage[jj * 64 + fe64] = __float2half_rn(silu_f32(gv) * uv);
-            }
-          }
-          named_bar(bar_id);
-          {
-            const int row = etid >> 3, ch = etid & 7;
-            if (row < nrow) {
-              *reinterpret_cast<uint4*>(C + size_t(row_base + c * 16 + row) * N + n0 + ch * 8) =
-                  *reinterpret_cast<const uint4*>(sCg + 4096 + row * 128 + ch * 16);
-            }
-          }
-          named_bar(bar_id);
         }
       }
       tc_fence_before();
@@ -572,7 +602,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    tmem_dealloc(tmem_base, 2 * kAccCols);
   }
 }
 
@@ -607,52 +637,44 @@ static int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
   return r == CUDA_SUCCESS ? LR_OK : LR_ERR_INVALID_ARGUMENT;
 }
 
-template <int BN, int MODE>
-static int launch_gemm(const CUtensorMap& tmap_a, const ExpertEntry* table, int E, int mat, int K,
-                       int N, const int32_t* seg_start, const int32_t* seg_len, int max_rows, int R,
+template <class S, int MODE>
+static int launch_gemm(const void* A, int K, int R, const ExpertEntry* table, int E, int mat,
+                       int N, const int32_t* seg_start, const int32_t* seg_len, int max_rows,
                        __half* C, int32_t* err, cudaStream_t stream) {
-  constexpr int STAGES = GemmStages<BN>::v;
-  constexpr int DSTAGES = GemmStages<BN>::d;
-  using L = GemmLayout<BN, STAGES, DSTAGES>;
-  static_assert(L::kTotal <= 227 * 1024, "shared memory budget");
-  auto kern = w4a16_grouped_gemm_kernel<BN, STAGES, DSTAGES, MODE>;
+  auto kern = w4a16_grouped_gemm_kernel<S, MODE>;
   static int configured = 0;
   if (!configured) {
-    LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
     configured = 1;
   }
+  CUtensorMap ta;
+  const int rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
+                           uint64_t(K) * 2, kBK, uint32_t(S::ROWS), CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
   int dev = 0, sms = 0;
   LR_CUDA_TRY(cudaGetDevice(&dev));
   LR_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  constexpr int BO = (MODE == LR_FFN_MODE_SWIGLU) ? 64 : 128;
+  constexpr int BO = (MODE == LR_FFN_MODE_SWIGLU) ? S::WN / 2 : S::WN;
   const long n_tiles = (N + BO - 1) / BO;
-  const long upper = long(E) * ((max_rows + BN - 1) / BN) * n_tiles;
+  const long upper = long(E) * ((max_rows + S::ROWS - 1) / S::ROWS) * n_tiles;
   const int grid = int(upper < sms ? (upper < 1 ? 1 : upper) : sms);
-  kern<<<grid, kGemmThreads, L::kTotal, stream>>>(tmap_a, table, E, mat, K, N, seg_start, seg_len,
+  kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, table, E, mat, K, N, seg_start, seg_len,
                                                   max_rows, R, C, err);
   LR_LAUNCH_CHECK();
   return LR_OK;
 }
 
+// Tile shape from the longest expert segment: 32 / 64 / 128 token rows with 256
+// weight columns, or 256 token rows (two stacked M sub-tiles) with 128.
 template <int MODE>
-static int dispatch_bn(int BN, const CUtensorMap& ta, const ExpertEntry* t, int E, int mat, int K,
-                       int N, const int32_t* ss, const int32_t* sl, int mr, int R, __half* C,
-                       int32_t* err, cudaStream_t st) {
-  switch (BN) {
-    case 16: return launch_gemm<16, MODE>(ta, t, E, mat, K, N, ss, sl, mr, R, C, err, st);
-    case 32: return launch_gemm<32, MODE>(ta, t, E, mat, K, N, ss, sl, mr, R, C, err, st);
-    case 64: return launch_gemm<64, MODE>(ta, t, E, mat, K, N, ss, sl, mr, R, C, err, st);
-    case 128: return launch_gemm<128, MODE>(ta, t, E, mat, K, N, ss, sl, mr, R, C, err, st);
-    default: return launch_gemm<256, MODE>(ta, t, E, mat, K, N, ss, sl, mr, R, C, err, st);
-  }
-}
-
-static int pick_bn(int max_rows) {
-  if (max_rows <= 16) return 16;
-  if (max_rows <= 32) return 32;
-  if (max_rows <= 64) return 64;
-  if (max_rows <= 128) return 128;
-  return 256;
+static int dispatch_shape(const void* A, int K, int R, const ExpertEntry* t, int E, int mat, int N,
+                          const int32_t* ss, const int32_t* sl, int mr, __half* C, int32_t* err,
+                          cudaStream_t st) {
+  if (mr <= 32) return launch_gemm<ShapeR32, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
+  if (mr <= 64) return launch_gemm<ShapeR64, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
+  if (mr <= 128)
+    return launch_gemm<ShapeR128, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
+  return launch_gemm<ShapeR256, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
 }
 
 }  // namespace lr
@@ -686,12 +708,14 @@ extern "C" int lr_encode_weight_table(const lr_expert_weights* experts, int E, i
       if ((reinterpret_cast<uintptr_t>(qw) | reinterpret_cast<uintptr_t>(experts[e].scales[m]) |
            reinterpret_cast<uintptr_t>(experts[e].zeros[m])) & 15u)
         return LR_ERR_INVALID_ARGUMENT;
-      int rc = encode_2d(&ent.qw16[m], CU_TENSOR_MAP_DATA_TYPE_INT32, qw, uint64_t(N / 8),
-                         uint64_t(K), uint64_t(N / 8) * 4, 16, kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
-      if (rc) return rc;
-      rc = encode_2d(&ent.qw8[m], CU_TENSOR_MAP_DATA_TYPE_INT32, qw, uint64_t(N / 8), uint64_t(K),
-                     uint64_t(N / 8) * 4, 8, kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
-      if (rc) return rc;
+      CUtensorMap* maps[3] = {&ent.qw32[m], &ent.qw16[m], &ent.qw8[m]};
+      const uint32_t words[3] = {32, 16, 8};
+      for (int b = 0; b < 3; ++b) {
+        const int rc = encode_2d(maps[b], CU_TENSOR_MAP_DATA_TYPE_INT32, qw, uint64_t(N / 8),
+                                 uint64_t(K), uint64_t(N / 8) * 4, words[b], kBK,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+      }
       ent.scales[m] = static_cast<const __half*>(experts[e].scales[m]);
       ent.zeros[m] = experts[e].zeros[m];
       ent.K[m] = K;
@@ -719,30 +743,26 @@ extern "C" int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, 
   if (mode < LR_FFN_MODE_PLAIN || mode > LR_FFN_MODE_SWIGLU) return LR_ERR_INVALID_ARGUMENT;
   if (mode != LR_FFN_MODE_SWIGLU && (mat < 0 || mat > 2)) return LR_ERR_INVALID_ARGUMENT;
   if (K < kBK || K % kBK != 0) return LR_ERR_UNSUPPORTED;
-  if (N < 32 || N % (mode == LR_FFN_MODE_SWIGLU ? 64 : 32) != 0) return LR_ERR_UNSUPPORTED;
+  if (N < 32 || N % 32 != 0) return LR_ERR_UNSUPPORTED;
   if (R < 0 || max_rows_per_expert < 0) return LR_ERR_INVALID_ARGUMENT;
   if (R == 0 || max_rows_per_expert == 0) return LR_OK;
   if (!A || !C || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(C)) & 15u))
     return LR_ERR_INVALID_ARGUMENT;
   if ((seg_start == nullptr) != (seg_len == nullptr)) return LR_ERR_INVALID_ARGUMENT;
   if (!seg_start && E != 1) return LR_ERR_INVALID_ARGUMENT;
-  const int BN = pick_bn(max_rows_per_expert);
-  CUtensorMap ta;
-  int rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
-                     uint64_t(K) * 2, kBK, uint32_t(BN), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
   const ExpertEntry* tab = static_cast<const ExpertEntry*>(device_table);
   __half* Cp = static_cast<__half*>(C);
+  const int mr = max_rows_per_expert;
   switch (mode) {
     case LR_FFN_MODE_PLAIN:
-      return dispatch_bn<LR_FFN_MODE_PLAIN>(BN, ta, tab, E, mat, K, N, seg_start, seg_len,
-                                            max_rows_per_expert, R, Cp, err, stream);
+      return dispatch_shape<LR_FFN_MODE_PLAIN>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr,
+                                               Cp, err, stream);
     case LR_FFN_MODE_SILU:
-      return dispatch_bn<LR_FFN_MODE_SILU>(BN, ta, tab, E, mat, K, N, seg_start, seg_len,
-                                           max_rows_per_expert, R, Cp, err, stream);
+      return dispatch_shape<LR_FFN_MODE_SILU>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp,
+                                              err, stream);
     default:
-      return dispatch_bn<LR_FFN_MODE_SWIGLU>(BN, ta, tab, E, mat, K, N, seg_start, seg_len,
-                                             max_rows_per_expert, R, Cp, err, stream);
+      return dispatch_shape<LR_FFN_MODE_SWIGLU>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr,
+                                                Cp, err, stream);
   }
 }
 
