@@ -261,6 +261,33 @@ LR_DEVICE void tmem_ld_32x32b_x16_sync(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 
+// Asynchronous form: issue the load now, consume the registers only after
+// tmem_ld_wait() on the same array (which ties them to the wait, so the compiler
+// cannot read them earlier).
+LR_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// tcgen05.wait::ld for every load issued so far; `r` (and `s`) pass through it.
+LR_DEVICE void tmem_ld_wait(uint32_t (&r)[16], uint32_t (&s)[16]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+        "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(s[0]), "+r"(s[1]), "+r"(s[2]), "+r"(s[3]),
+        "+r"(s[4]), "+r"(s[5]), "+r"(s[6]), "+r"(s[7]), "+r"(s[8]), "+r"(s[9]), "+r"(s[10]),
+        "+r"(s[11]), "+r"(s[12]), "+r"(s[13]), "+r"(s[14]), "+r"(s[15])
+      :
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 format, version 1).
 //   start address, leading byte offset and stride byte offset are in 16-byte units;
 //   layout 2 = 128-byte swizzle.
@@ -290,6 +317,9 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int a_mn_maj
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------
-LR_DEVICE float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
+// x * sigmoid(x) with the fast intrinsics (__expf, __fdividef: a few ulp in fp32,
+// far below the fp16 rounding of the GEMM output).  For x below about -88,
+// __expf(-x) is +inf and __fdividef returns 0.
+LR_DEVICE float silu_f32(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 }  // namespace lr

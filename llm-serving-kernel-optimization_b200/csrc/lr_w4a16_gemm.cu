@@ -42,16 +42,19 @@ constexpr int kDeqWarps = 8;
 constexpr int kProdWarp = kEpiWarps + kDeqWarps;
 constexpr int kMmaWarp = kProdWarp + 1;
 constexpr int kGemmThreads = (kMmaWarp + 1) * 32;
-constexpr int kAccCols = 256;  // TMEM columns per accumulator (MT * WN)
 
 // Tile shape: MT sub-tiles of 128 M rows (TOKROWS loaded per sub-tile) x WN
 // weight columns; STAGES TMA stages (tokens + packed weights), DSTAGES
-// dequantized-operand buffers and DGROUPS dequant warp groups.
-template <int TOKROWS_, int MT_, int STAGES_, int DSTAGES_, int DGROUPS_>
+// dequantized-operand buffers and DGROUPS dequant warp groups.  The
+// accumulator takes MT * WN TMEM columns; it is double buffered when two fit
+// in the 512 columns of an SM, otherwise the epilogue of a tile and the main
+// loop of the next one take turns.
+template <int TOKROWS_, int MT_, int WN_, int STAGES_, int DSTAGES_, int DGROUPS_>
 struct GemmShape {
-  static constexpr int TOKROWS = TOKROWS_, MT = MT_, STAGES = STAGES_, DSTAGES = DSTAGES_,
-                       DGROUPS = DGROUPS_;
-  static constexpr int WN = kAccCols / MT;             // weight columns per tile (UMMA N)
+  static constexpr int TOKROWS = TOKROWS_, MT = MT_, WN = WN_, STAGES = STAGES_,
+                       DSTAGES = DSTAGES_, DGROUPS = DGROUPS_;
+  static constexpr int ACC = MT * WN;                  // TMEM columns per accumulator
+  static constexpr int NACC = 2 * ACC <= 512 ? 2 : 1;  // accumulator buffers
   static constexpr int WJ = WN / 8;                    // packed words per weight row
   static constexpr int ROWS = MT * TOKROWS;            // token rows per tile
   // UMMA M: 64 when a single sub-tile loads at most 64 rows.  An M = 64
@@ -76,12 +79,17 @@ struct GemmShape {
   static_assert(ROWS <= 256, "TMA box height");
   static_assert(kDeqWarps % DGROUPS == 0 && DGROUPS <= DSTAGES, "dequant groups");
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
+  static_assert(NACC * ACC <= 512 && WN % 64 == 0 && WN <= 256, "TMEM accumulators");
 };
 
-using ShapeR32 = GemmShape<32, 1, 7, 4, 4>;
-using ShapeR64 = GemmShape<64, 1, 5, 4, 4>;
-using ShapeR128 = GemmShape<128, 1, 6, 2, 2>;
-using ShapeR256 = GemmShape<128, 2, 4, 4, 2>;
+using ShapeR32 = GemmShape<32, 1, 256, 7, 4, 4>;
+using ShapeR64 = GemmShape<64, 1, 256, 5, 4, 4>;
+using ShapeR128 = GemmShape<128, 1, 256, 6, 2, 2>;
+using ShapeR256 = GemmShape<128, 2, 128, 4, 4, 2>;   // double-buffered accumulator
+using ShapeR256W = GemmShape<128, 2, 256, 3, 3, 2>;  // 256x256 tile, one accumulator
+// K at and above which the 256x256 tile pays: its epilogue is not overlapped
+// with the next tile's main loop, so it needs enough k-steps to amortise.
+constexpr int kWideTileMinK = 4096;
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -135,7 +143,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(s_tmem, 2 * kAccCols);
+    tmem_alloc(s_tmem, S::NACC * S::ACC);
     tmem_relinquish();
   }
   if (warp == kProdWarp) {
@@ -216,14 +224,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // issued; a blocking wait is needed only when the test came back false.
       bool pre_full = false, pre_dfull = false;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
-        const int acc = lt & 1;
-        const uint32_t aph = (lt >> 1) & 1;
+        const int acc = S::NACC == 2 ? (lt & 1) : 0;
+        const uint32_t aph = S::NACC == 2 ? (lt >> 1) & 1 : lt & 1;
         if (!wait_any(&tempty[acc], aph ^ 1, s_abort, err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * kAccCols);
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * S::ACC);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -391,8 +399,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++lt) {
       int e, mt, nt;
       decode(tile, e, mt, nt);
-      const int acc = lt & 1;
-      const uint32_t aph = (lt >> 1) & 1;
+      const int acc = S::NACC == 2 ? (lt & 1) : 0;
+      const uint32_t aph = S::NACC == 2 ? (lt >> 1) & 1 : lt & 1;
       // a group leaves together: the barrier reduces "any wait failed"
       const bool waited = wait_any(&tfull[acc], aph, s_abort, err);
       if (named_bar_any(1 + grp, !waited)) {
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int rows_valid = min(ROWS, s_len[e] - mt * ROWS);
       const int row0 = s_start[e] + mt * ROWS;
       const int n0 = nt * BO;
-      const uint32_t tacc = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * kAccCols);
+      const uint32_t tacc = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * S::ACC);
       // TMEM lane = token row (M = 64: lanes 0-15 of each quarter), column =
       // weight column.  MT = 2: group g drains sub-tile g (all chunks); MT = 1:
       // the groups take alternate chunks.
@@ -414,15 +422,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __half* crow = C + size_t(row0 + (row_ok ? trow : 0)) * N;
       const uint32_t tbase = tacc + uint32_t(msub * WN);
       if (quarter * RQ < S::TOKROWS && msub * 128 + quarter * RQ < rows_valid) {
-        for (int c = MT == 2 ? 0 : grp; c < BO / 16; c += MT == 2 ? 1 : 2) {
-          const int f0 = n0 + c * 16;
-          if (f0 >= N) break;
-          uint32_t v[16];
+        // chunk c: accumulator columns 16c.. (SwiGLU: gate 16c.., up WN/2 + 16c..).
+        // The loads of the next chunk are in flight while this one is converted
+        // and stored.
+        const int c0 = MT == 2 ? 0 : grp;
+        constexpr int cstep = MT == 2 ? 1 : 2;
+        const int cend = min(BO / 16, (N - n0 + 15) / 16);
+        uint32_t v[16], u[16];
+        if (c0 < cend) {
+          tmem_ld_32x32b_x16(tbase + c0 * 16, v);
+          if (kGLU) tmem_ld_32x32b_x16(tbase + WN / 2 + c0 * 16, u);
+          tmem_ld_wait(v, u);
+        }
+        for (int c = c0; c < cend; c += cstep) {
           float f[16];
-          tmem_ld_32x32b_x16_sync(tbase + c * 16, v);
           if (kGLU) {
-            uint32_t u[16];
-            tmem_ld_32x32b_x16_sync(tbase + WN / 2 + c * 16, u);
 #pragma unroll
             for (int i = 0; i < 16; ++i)
               f[i] = silu_f32(__uint_as_float(v[i])) * __uint_as_float(u[i]);
@@ -433,11 +447,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (MODE == LR_FFN_MODE_SILU) f[i] = silu_f32(f[i]);
             }
           }
+          const bool more = c + cstep < cend;
+          if (more) {
+            tmem_ld_32x32b_x16(tbase + (c + cstep) * 16, v);
+            if (kGLU) tmem_ld_32x32b_x16(tbase + WN / 2 + (c + cstep) * 16, u);
+          }
           if (row_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + f0);
+            uint4* dst = reinterpret_cast<uint4*>(crow + n0 + c * 16);
             dst[0] = pack8_feature_order(f);
             dst[1] = pack8_feature_order(f + 8);
           }
+          if (more) tmem_ld_wait(v, u);
         }
       }
       tc_fence_before();
@@ -447,7 +467,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * kAccCols);
+    tmem_dealloc(tmem_base, S::NACC * S::ACC);
   }
 }
 
@@ -482,7 +502,8 @@ static int launch_gemm(const void* A, int K, int R, const ExpertEntry* table, in
 }
 
 // Tile shape from the longest expert segment: 32 / 64 / 128 token rows with 256
-// weight columns, or 256 token rows (two stacked M sub-tiles) with 128.
+// weight columns, or 256 token rows (two stacked M sub-tiles) with 128 weight
+// columns (double-buffered accumulator) or, for long K, 256.
 template <int MODE>
 static int dispatch_shape(const void* A, int K, int R, const ExpertEntry* t, int E, int mat, int N,
                           const int32_t* ss, const int32_t* sl, int mr, __half* C, int32_t* err,
@@ -491,6 +512,8 @@ static int dispatch_shape(const void* A, int K, int R, const ExpertEntry* t, int
   if (mr <= 64) return launch_gemm<ShapeR64, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
   if (mr <= 128)
     return launch_gemm<ShapeR128, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
+  if (K >= kWideTileMinK)
+    return launch_gemm<ShapeR256W, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
   return launch_gemm<ShapeR256, MODE>(A, K, R, t, E, mat, N, ss, sl, mr, C, err, st);
 }
 

@@ -129,6 +129,33 @@ def test_grouped_modes(mode, lens, maxr):
     assert torch.equal(out[~covered], sentinel[~covered])
 
 
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_grouped_wide_tile_long_k(mode):
+    """K >= 4096 with segments over 128 rows: the 256x256 tile with one accumulator
+    (epilogue and next main loop take turns), ragged rows and a feature tail."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E, d, f, g = 3, 4096, 320, 64   # every matrix needs K % g == 0 (d_ff = 320 for the down)
+    lens = [300, 0, 129]
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, mode, seed=41 + mode)
+    sentinel = torch.full((R, f), 5.0, dtype=torch.float16, device=DEV)
+    out = grouped_w4a16(table, E, mode, 1, A, f, ss, sl, 300, out=sentinel.clone())
+    covered = torch.zeros(R, dtype=torch.bool, device=DEV)
+    for e, L in enumerate(lens):
+        st = int(ss[e])
+        if L == 0:
+            continue
+        x = A[st:st + L].float()
+        if mode == 0:
+            ref = x @ deq[e][1].float()
+        elif mode == 1:
+            ref = torch.nn.functional.silu(x @ deq[e][1].float())
+        else:
+            ref = torch.nn.functional.silu(x @ deq[e][0].float()) * (x @ deq[e][1].float())
+        _check(out[st:st + L], ref)
+        covered[st:st + L] = True
+    assert torch.equal(out[~covered], sentinel[~covered])
+
+
 def test_grouped_down_projection_long_k():
     """K = d_ff = 14336 (the Mixtral down projection), a few rows per expert."""
     from lightning_router.kernels.quantized_matmul import grouped_w4a16, weight_table
