@@ -205,6 +205,54 @@ int lr_quantized_matmul(const void* device_table, const void* A, int M, int K, i
                         void* C, void* workspace, size_t workspace_bytes, int32_t* err,
                         lr_stream_t stream);
 
+/* ---- expert-parallel exchange over NVLink peer memory --------------------
+ * Replaces the all-GPU expert execution + host all-reduce of the reference's
+ * serving worker (lightning_router/serving/worker.py:156-186) for one process
+ * per GPU.  Rank r owns experts [r*E/G, (r+1)*E/G).  The caller keeps three
+ * buffers per rank mapped by every other rank (lr_ipc_*): the rank's tokens,
+ * the row -> token map of its uncapped expert segments (source_idx of
+ * lr_permute_tokens without rows) and the expert-output rows it computes;
+ * peer_* are device arrays of the G ranks' addresses of such a buffer.
+ * Ordering across GPUs is the caller's: a collective after the tokens and
+ * maps are written (the counts all-gather) before lr_ep_gather, and one after
+ * the expert outputs are written before lr_ep_combine.                       */
+
+/* Number of int32 entries of an exchange plan. */
+int lr_ep_plan_size(int world, int num_experts);
+
+/* plan from counts[G][E] (slots of each expert on each rank, uncapped): the
+ * global slot-order capacity (kept(r, e) = clamp(C - sum_{r'<r} counts[r'][e],
+ * 0, counts[r][e]), the single-GPU rule), the owner's segments [local expert]
+ * [source rank] and where this rank's kept rows land at every owner.
+ * Limits: G * E <= 4096.                                                     */
+int lr_ep_plan(const int32_t* counts, int world, int num_experts, int rank, int capacity,
+               int32_t* plan, int32_t* err, lr_stream_t stream);
+
+/* Expert owner: rows of its segments <- the kept token rows, read from the
+ * source ranks' token buffers (tokens < max_tokens, map entries < max_slots).
+ * out has rows_max = E/G * capacity rows of d fp16; rows past the segments are
+ * not written.                                                               */
+int lr_ep_gather(const uint64_t* peer_tokens, const uint64_t* peer_source_idx,
+                 const int32_t* plan, int world, int num_experts, int rank, int max_tokens,
+                 int max_slots, int d, int rows_max, void* out, int32_t* err,
+                 lr_stream_t stream);
+
+/* Token owner: out[t,:] = fp16( sum_j gate_weights[t*k+j] * y_owner[row, :] )
+ * over the kept slots in slot order (fp32), y read from the owners' expert
+ * output buffers; slot_pos holds each slot's uncapped local row.             */
+int lr_ep_combine(const uint64_t* peer_outputs, const int32_t* plan, const int32_t* expert_ids,
+                  const float* gate_weights, const int32_t* slot_pos, int T, int k, int world,
+                  int num_experts, int d, int rows_max, void* out, int32_t* err,
+                  lr_stream_t stream);
+
+/* CUDA IPC of a device buffer: export writes a 64-byte handle of the buffer's
+ * allocation and the buffer's offset in it; import (in another process) maps
+ * the allocation and returns the buffer address (+ the mapping base, which
+ * lr_ipc_close unmaps).                                                      */
+int lr_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int lr_ipc_import(const void* handle, uint64_t offset, void** ptr, void** base);
+int lr_ipc_close(void* base);
+
 #ifdef __cplusplus
 }
 #endif

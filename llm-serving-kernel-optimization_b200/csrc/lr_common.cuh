@@ -314,6 +314,39 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int a_mn_maj
          | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+constexpr int kMaxTopK = 8;  // largest top-k of the routing kernels
+
+// ---------------------------------------------------------------------------
+// 16-byte rows of fp16
+// ---------------------------------------------------------------------------
+// Streaming read of data that is read once (no L1 allocation, read-only path).
+LR_DEVICE uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// a[i] += w * v[i] for the eight fp16 values of v, fp32 fused multiply-add.
+LR_DEVICE void acc_half8(float (&a)[8], const uint4& v, float w) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    a[2 * i] = fmaf(w, f.x, a[2 * i]);
+    a[2 * i + 1] = fmaf(w, f.y, a[2 * i + 1]);
+  }
+}
+
+LR_DEVICE uint4 pack_half8(const float (&a)[8]) {
+  uint4 o;
+  __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(a[2 * i], a[2 * i + 1]);
+  return o;
+}
+
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------

@@ -23,7 +23,6 @@ namespace lr {
 
 constexpr int kRouteThreads = 256;   // tokens per block of the gating route kernel
 constexpr int kSlotBlock = 1024;     // slots per block of the given-ids route kernel
-constexpr int kMaxTopK = 8;
 constexpr int kWarps = kRouteThreads / 32;
 
 // ---------------------------------------------------------------------------
@@ -405,14 +404,6 @@ __global__ void __launch_bounds__(kRouteThreads)
 // ---------------------------------------------------------------------------
 // permute
 // ---------------------------------------------------------------------------
-LR_DEVICE uint4 ld_stream(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
 constexpr int kCopyUnroll = 8;
 
 // gated routing: one warp per token, the row is read once and written k times.
@@ -535,24 +526,6 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------
 // combine: one warp per token, fp32 accumulation in slot order
 // ---------------------------------------------------------------------------
-LR_DEVICE void acc_half8(float (&a)[8], const uint4& v, float w) {
-  const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    a[2 * i] = fmaf(w, f.x, a[2 * i]);
-    a[2 * i + 1] = fmaf(w, f.y, a[2 * i + 1]);
-  }
-}
-
-LR_DEVICE uint4 pack_half8(const float (&a)[8]) {
-  uint4 o;
-  __half2* h = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(a[2 * i], a[2 * i + 1]);
-  return o;
-}
-
 constexpr int kCombUnroll = 4;
 
 __global__ void __launch_bounds__(256)

@@ -335,6 +335,87 @@ at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int6
   return C;
 }
 
+// Routing without rows: every slot's uncapped local row (slot_pos) and the
+// row -> token map (source_idx, S entries) of this shard's expert segments.
+at::Tensor route_rows(const at::Tensor& expert_ids, const at::Tensor& gate_weights,
+                      const at::Tensor& row_offsets, at::Tensor slot_pos, const at::Tensor& ws,
+                      int64_t num_tokens, int64_t num_experts, at::Tensor source_idx) {
+  check_cuda(expert_ids, "expert_ids");
+  const int64_t S = expert_ids.numel();
+  TORCH_CHECK(num_tokens > 0 && S % num_tokens == 0, "slot count must be T*k");
+  TORCH_CHECK(row_offsets.numel() == num_experts + 1, "row_offsets: (E+1,)");
+  TORCH_CHECK(source_idx.scalar_type() == at::kInt && source_idx.numel() >= S &&
+                  source_idx.is_contiguous(),
+              "source_idx: >= S contiguous int32");
+  c10::cuda::CUDAGuard g(expert_ids.device());
+  auto rw = at::empty({S}, expert_ids.options().dtype(at::kFloat));
+  check_status(lr_permute_tokens(nullptr, int(num_tokens), 0, int(num_experts),
+                                 int(S / num_tokens), int(S), expert_ids.data_ptr<int32_t>(),
+                                 gate_weights.data_ptr<float>(), row_offsets.data_ptr<int32_t>(),
+                                 nullptr, 0, 0, slot_pos.data_ptr<int32_t>(), nullptr,
+                                 rw.data_ptr<float>(), source_idx.data_ptr<int32_t>(),
+                                 ws.data_ptr(), size_t(ws.numel()), cur_stream()),
+               "route_rows");
+  return rw;
+}
+
+at::Tensor ep_plan(const at::Tensor& counts, int64_t rank, int64_t capacity,
+                   const c10::optional<at::Tensor>& err) {
+  check_cuda(counts, "counts");
+  TORCH_CHECK(counts.dim() == 2 && counts.scalar_type() == at::kInt && counts.is_contiguous(),
+              "counts: contiguous (G, E) int32");
+  c10::cuda::CUDAGuard g(counts.device());
+  const int G = int(counts.size(0)), E = int(counts.size(1));
+  const int n = lr_ep_plan_size(G, E);
+  TORCH_CHECK(n > 0, "ep_plan: E must be a multiple of G");
+  auto plan = at::empty({n}, counts.options());
+  check_status(lr_ep_plan(counts.data_ptr<int32_t>(), G, E, int(rank), int(capacity),
+                          plan.data_ptr<int32_t>(), err_ptr(err), cur_stream()),
+               "ep_plan");
+  return plan;
+}
+
+at::Tensor ep_gather(const at::Tensor& peer_tokens, const at::Tensor& peer_source_idx,
+                     const at::Tensor& plan, int64_t num_experts, int64_t rank,
+                     int64_t max_tokens, int64_t max_slots, int64_t d, at::Tensor out,
+                     const c10::optional<at::Tensor>& err) {
+  check_cuda(plan, "plan");
+  check_cuda(out, "out");
+  TORCH_CHECK(peer_tokens.scalar_type() == at::kLong && peer_source_idx.scalar_type() == at::kLong,
+              "peer address arrays: int64");
+  TORCH_CHECK(out.scalar_type() == at::kHalf && out.dim() == 2 && out.size(1) == d &&
+                  out.is_contiguous(),
+              "out: contiguous (rows, d) fp16");
+  c10::cuda::CUDAGuard g(out.device());
+  check_status(lr_ep_gather(reinterpret_cast<const uint64_t*>(peer_tokens.data_ptr()),
+                            reinterpret_cast<const uint64_t*>(peer_source_idx.data_ptr()),
+                            plan.data_ptr<int32_t>(), int(peer_tokens.numel()), int(num_experts),
+                            int(rank), int(max_tokens), int(max_slots), int(d),
+                            int(out.size(0)), out.data_ptr(), err_ptr(err), cur_stream()),
+               "ep_gather");
+  return out;
+}
+
+at::Tensor ep_combine(const at::Tensor& peer_outputs, const at::Tensor& plan,
+                      const at::Tensor& expert_ids, const at::Tensor& gate_weights,
+                      const at::Tensor& slot_pos, int64_t num_tokens, int64_t num_experts,
+                      int64_t rows_max, int64_t d, const c10::optional<at::Tensor>& err) {
+  check_cuda(plan, "plan");
+  TORCH_CHECK(peer_outputs.scalar_type() == at::kLong, "peer address array: int64");
+  const int64_t S = expert_ids.numel();
+  TORCH_CHECK(num_tokens >= 0 && (num_tokens == 0 || S % num_tokens == 0), "slot count");
+  c10::cuda::CUDAGuard g(plan.device());
+  auto out = at::empty({num_tokens, d}, plan.options().dtype(at::kHalf));
+  const int k = num_tokens ? int(S / num_tokens) : 1;
+  check_status(lr_ep_combine(reinterpret_cast<const uint64_t*>(peer_outputs.data_ptr()),
+                             plan.data_ptr<int32_t>(), expert_ids.data_ptr<int32_t>(),
+                             gate_weights.data_ptr<float>(), slot_pos.data_ptr<int32_t>(),
+                             int(num_tokens), k, int(peer_outputs.numel()), int(num_experts),
+                             int(d), int(rows_max), out.data_ptr(), err_ptr(err), cur_stream()),
+               "ep_combine");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(lightning_router, m) {
@@ -362,6 +443,17 @@ TORCH_LIBRARY(lightning_router, m) {
   m.def(
       "grouped_w4a16_gemm(Tensor table, int num_experts, int mode, int mat, Tensor A, int N, "
       "Tensor? seg_start, Tensor? seg_len, int max_rows, Tensor? out, Tensor? err) -> Tensor");
+  m.def(
+      "route_rows(Tensor expert_ids, Tensor gate_weights, Tensor row_offsets, Tensor(a!) "
+      "slot_pos, Tensor ws, int num_tokens, int num_experts, Tensor(b!) source_idx) -> Tensor");
+  m.def("ep_plan(Tensor counts, int rank, int capacity, Tensor? err) -> Tensor");
+  m.def(
+      "ep_gather(Tensor peer_tokens, Tensor peer_source_idx, Tensor plan, int num_experts, "
+      "int rank, int max_tokens, int max_slots, int d, Tensor(a!) out, Tensor? err) -> Tensor");
+  m.def(
+      "ep_combine(Tensor peer_outputs, Tensor plan, Tensor expert_ids, Tensor gate_weights, "
+      "Tensor slot_pos, int num_tokens, int num_experts, int rows_max, int d, Tensor? err) -> "
+      "Tensor");
 }
 
 TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
@@ -373,6 +465,10 @@ TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
   m.impl("permute_tokens", &permute_tokens);
   m.impl("expert_routing_gather", &expert_routing_gather);
   m.impl("grouped_w4a16_gemm", &grouped_w4a16_gemm);
+  m.impl("route_rows", &route_rows);
+  m.impl("ep_plan", &ep_plan);
+  m.impl("ep_gather", &ep_gather);
+  m.impl("ep_combine", &ep_combine);
 }
 
 TORCH_LIBRARY_IMPL(lightning_router, CompositeExplicitAutograd, m) {

@@ -142,9 +142,11 @@ class ExpertGroup(nn.Module):
 
     def forward_segments(self, x: torch.Tensor, seg_start: torch.Tensor, seg_len: torch.Tensor,
                          max_rows: int, first_expert: int = 0,
-                         num_local: int | None = None, mark=None) -> torch.Tensor:
+                         num_local: int | None = None, mark=None,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
         """Rows ``[seg_start[e], seg_start[e] + seg_len[e])`` of ``x`` through expert
-        ``first_expert + e``; other rows of the result are left unwritten."""
+        ``first_expert + e``; other rows of the result (``out`` if given, with as many
+        rows as ``x``) are left unwritten."""
         if not self.quantized:
             raise RuntimeError("forward_segments requires quantized experts")
         n = self.num_experts - first_expert if num_local is None else num_local
@@ -160,7 +162,8 @@ class ExpertGroup(nn.Module):
                           seg_len, max_rows, out=h)
         if mark is not None:
             mark("ffn_in")
-        y = torch.empty(R, self.hidden_size, dtype=torch.float16, device=x.device)
+        y = torch.empty(R, self.hidden_size, dtype=torch.float16, device=x.device) \
+            if out is None else out
         grouped_w4a16(table, n, FFN_MODE_PLAIN, 2, h, self.hidden_size, seg_start, seg_len,
                       max_rows, out=y)
         if mark is not None:

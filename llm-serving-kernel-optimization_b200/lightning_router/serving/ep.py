@@ -22,15 +22,28 @@ the single-GPU output.  Here the experts are sharded and tokens move:
   over all ranks and micro-batches).
 
 Every kept row goes through the same per-row arithmetic as on one GPU, so the
-output equals the single-GPU output bit for bit.  The exchange needs the split
-sizes on the host: one device->host read of the gathered counts per forward.
+output equals the single-GPU output bit for bit.
 
-:func:`plan_exchange` is the pure host part (no GPU); it is exercised by CPU
-``gloo`` tests against the oracle.
+Two exchanges implement the moves:
+
+* ``exchange="peer"`` (default with one process per GPU on one node): every rank
+  keeps its tokens, the row -> token map of its expert segments and its expert
+  outputs in buffers the other ranks map through CUDA IPC.  The plan is made on
+  the device from the all-gathered counts (``lr_ep_plan``), the expert owner
+  pulls its kept rows over NVLink (``lr_ep_gather``) and the token owner pulls
+  the output rows back while it combines them (``lr_ep_combine``).  No host
+  synchronisation; the counts all-gather and one 4-byte all-reduce after the
+  expert GEMMs order the peer reads.  Token shards must have equal sizes.
+* ``exchange="nccl"``: kept rows are permuted into a compact send buffer grouped
+  by owner rank, exchanged with ``all_to_all_single`` and sent back the same
+  way.  The split sizes need one device->host read of the gathered counts per
+  forward (:func:`plan_exchange`, the pure host part, exercised by CPU ``gloo``
+  tests against the oracle).
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -126,18 +139,80 @@ def plan_exchange(stats: np.ndarray, rank: int, world: int, num_experts: int, to
                           load_balance_weight, nchunks)[chunk]
 
 
+class _PeerBuffers:
+    """Per-rank exchange buffers mapped by every rank of the group (CUDA IPC).
+
+    ``x`` (T_max, d) tokens and ``src`` (T_max*k) row -> token map are read by the
+    expert owners; ``y`` (rows_max, d) expert outputs are read by the token owners;
+    ``a`` (rows_max, d) is this rank's GEMM input (local).  ``p*`` hold the G
+    ranks' addresses of each mapped buffer (int64, on the device).
+    """
+
+    def __init__(self, group, world: int, rank: int, dev, T_max: int, k: int, d: int,
+                 rows_max: int):
+        self.T_max, self.rows_max = T_max, rows_max
+        self.x = torch.empty(T_max, d, dtype=torch.float16, device=dev)
+        self.src = torch.zeros(T_max * k, dtype=torch.int32, device=dev)
+        self.y = torch.empty(max(rows_max, 1), d, dtype=torch.float16, device=dev)
+        self.a = torch.empty(max(rows_max, 1), d, dtype=torch.float16, device=dev)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        lib = _ext.clib()
+        mine = []
+        for t in (self.x, self.src, self.y):
+            h = ctypes.create_string_buffer(64)
+            off = ctypes.c_uint64(0)
+            _check(lib.lr_ipc_export(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)),
+                   "lr_ipc_export")
+            mine.append((h.raw, int(off.value)))
+        allh = [None] * world
+        dist.all_gather_object(allh, mine, group=group)
+        self._bases = []
+        ptrs = [[0] * world for _ in range(3)]
+        for r in range(world):
+            for b, t in enumerate((self.x, self.src, self.y)):
+                if r == rank:
+                    ptrs[b][r] = t.data_ptr()
+                    continue
+                hb, off = allh[r][b]
+                p, base = ctypes.c_void_p(), ctypes.c_void_p()
+                _check(lib.lr_ipc_import(ctypes.create_string_buffer(hb, 64), ctypes.c_uint64(off),
+                                         ctypes.byref(p), ctypes.byref(base)), "lr_ipc_import")
+                self._bases.append(base.value)
+                ptrs[b][r] = p.value
+        self.px, self.psrc, self.py = (torch.tensor(p, dtype=torch.int64, device=dev)
+                                       for p in ptrs)
+
+    def close(self) -> None:
+        lib = _ext.clib()
+        for b in self._bases:
+            lib.lr_ipc_close(ctypes.c_void_p(b))
+        self._bases = []
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        msg = _ext.clib().lr_status_string(status)
+        raise RuntimeError(f"{what} failed: {msg.decode() if isinstance(msg, bytes) else msg}")
+
+
 class ExpertParallelMoE:
     """Expert-parallel forward of a ``MoELayer`` (one rank per GPU).
 
     ``layer`` must hold at least this rank's experts; the other experts'
     buffers are not read.  ``forward(x_local)`` takes this rank's token shard
     (T_r, d) fp16 and returns ``(out_local, aux_loss)`` for the whole job's
-    routing (aux is the global load-balancing loss).
+    routing (aux is the global load-balancing loss).  ``exchange`` selects the
+    token exchange ("peer" or "nccl", see the module notes); ``microbatches``
+    applies to the NCCL exchange.
     """
 
-    def __init__(self, layer, world: int, rank: int, group=None, microbatches: int = 1):
+    def __init__(self, layer, world: int, rank: int, group=None, microbatches: int = 1,
+                 exchange: str = "peer"):
         if layer.num_experts % world:
             raise ValueError("num_experts must be divisible by the world size")
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"exchange must be 'peer' or 'nccl', got {exchange!r}")
+        self.exchange = exchange
         self.layer = layer
         self.world = world
         self.rank = rank
@@ -151,6 +226,9 @@ class ExpertParallelMoE:
         self.stage_events: list | None = None
         self._last_recv = 0
         self._pinned: torch.Tensor | None = None  # reused host staging for per-step metadata
+        self._peer: _PeerBuffers | None = None
+        self._peer_key = None
+        self._plan: torch.Tensor | None = None
 
     def _to_device(self, arr: np.ndarray, dev, dtype) -> torch.Tensor:
         """Copy a small host array to the device through a persistent pinned buffer."""
@@ -169,9 +247,16 @@ class ExpertParallelMoE:
         return out
 
     @classmethod
-    def from_layer(cls, layer, world: int, rank: int, group=None,
-                   microbatches: int = 1) -> "ExpertParallelMoE":
-        return cls(layer, world, rank, group, microbatches)
+    def from_layer(cls, layer, world: int, rank: int, group=None, microbatches: int = 1,
+                   exchange: str = "peer") -> "ExpertParallelMoE":
+        return cls(layer, world, rank, group, microbatches, exchange)
+
+    def close(self) -> None:
+        """Unmap the peers' exchange buffers (call before destroying the group)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+            self._peer_key = None
 
     def _mark(self, name):
         if self.stage_events is not None:
@@ -180,10 +265,81 @@ class ExpertParallelMoE:
             self.stage_events.append((name, ev))
 
     def last_kept_rows(self) -> int:
+        if self.exchange == "peer" and self._plan is not None:
+            return int(self._plan[self.El:2 * self.El].sum())
         return self._last_recv
+
+    def _peer_buffers(self, T_l: int, d: int, dev) -> _PeerBuffers | None:
+        """Exchange buffers for this shard size (a collective when the size changes:
+        all ranks call forward with their new shards together).  None when the
+        shards differ in size (the NCCL exchange handles that)."""
+        key = (T_l, d, dev.index)
+        if self._peer_key != key:
+            sizes = [None] * self.world
+            dist.all_gather_object(sizes, T_l, group=self.group)
+            self.close()
+            self._peer_key = key
+            if any(t != T_l for t in sizes):
+                return None
+            C = expert_capacity(T_l * self.world * self.k, self.E, self.cf)
+            self._peer = _PeerBuffers(self.group, self.world, self.rank, dev, T_l, self.k, d,
+                                      self.El * C)
+            self._peer_C = C
+        return self._peer
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor):
+        if self.exchange == "peer" and self.world > 1:
+            xf = x.reshape(-1, x.shape[-1])
+            bufs = self._peer_buffers(xf.shape[0], xf.shape[1], xf.device)
+            if bufs is not None:
+                return self._forward_peer(xf, bufs)
+        return self._forward_nccl(x)
+
+    def _forward_peer(self, x: torch.Tensor, bufs: _PeerBuffers):
+        ops = _ext.ops()
+        dev = x.device
+        x = x.to(torch.float16).contiguous()
+        T_l, d = x.shape
+        E, G, El, k = self.E, self.world, self.El, self.k
+        C = self._peer_C
+        err = _ext.error_word(dev.index)
+        self._mark("begin")
+        logits = self.layer.gate.logits(x)
+        self._mark("gate")
+        ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = ops.topk_route(logits, k, 1,
+                                                                         float(self.lbw), err)
+        # this rank's tokens and its uncapped row -> token map, readable by the owners
+        bufs.x[:T_l].copy_(x)
+        ops.route_rows(ids, gw, offs, pos, ws, T_l, E, bufs.src)
+        stats_l = torch.cat([torch.full((1,), float(T_l), dtype=torch.float64, device=dev),
+                             (offs[1:] - offs[:-1]).double(), psum])
+        stats = torch.empty(G * stats_l.numel(), dtype=torch.float64, device=dev)
+        # after the writes above on every rank: the gather below may read them
+        dist.all_gather_into_tensor(stats, stats_l, group=self.group)
+        st = stats.view(G, -1)
+        counts = st[:, 1:1 + E].round().to(torch.int32).contiguous()
+        plan = ops.ep_plan(counts, self.rank, C, err)
+        a = ops.ep_gather(bufs.px, bufs.psrc, plan, E, self.rank, bufs.T_max, bufs.T_max * k,
+                          d, bufs.a, err)
+        self._mark("dispatch")
+        self.layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C,
+                                            first_expert=self.rank * El, num_local=El,
+                                            mark=self._mark, out=bufs.y)
+        # every owner's outputs are written before any rank reads them
+        dist.all_reduce(bufs.flag, group=self.group)
+        self._mark("a2a_combine")
+        out = ops.ep_combine(bufs.py, plan, ids, gw, pos, T_l, E, bufs.rows_max, d, err)
+        self._mark("combine")
+        S = T_l * G * k
+        f = counts.sum(0).double() / float(max(S, 1))
+        P = st[:, 1 + E:].sum(0) / float(max(T_l * G, 1))
+        aux = (self.lbw * E * (f * P).sum()).float()
+        self._plan = plan
+        return out, aux
+
+    @torch.no_grad()
+    def _forward_nccl(self, x: torch.Tensor):
         ops = _ext.ops()
         dev = x.device
         x = x.reshape(-1, x.shape[-1]).to(torch.float16).contiguous()

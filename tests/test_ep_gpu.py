@@ -30,7 +30,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, wname, overrides, q):
+def _worker(rank, world, port, wname, overrides, exchange, q):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -43,7 +43,7 @@ def _worker(rank, world, port, wname, overrides, q):
         w = dataclasses.replace(WORKLOADS[wname], **overrides)
         layer, t = build_layer(w, device=dev)
         Tl = w.tokens // world
-        ep = ExpertParallelMoE.from_layer(layer, world, rank)
+        ep = ExpertParallelMoE.from_layer(layer, world, rank, exchange=exchange)
         out, aux = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
         out2, _ = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
         same = bool(torch.equal(out, out2))
@@ -55,23 +55,25 @@ def _worker(rank, world, port, wname, overrides, q):
             q.put(("ok", bool(torch.equal(full, ref)), float((full.float() - ref.float()).abs().max()),
                    float(aux), float(ref_aux), same))
         dist.barrier()
+        ep.close()
         dist.destroy_process_group()
     except Exception:
         q.put(("err", traceback.format_exc(), None, None, None, None))
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("wname,overrides", [
     ("prefill", dict(tokens=2048, d_model=1024, d_ff=2048)),
     ("fine", dict(tokens=1024, d_model=512)),
 ])
-def test_expert_parallel_matches_single_gpu(world, wname, overrides):
+def test_expert_parallel_matches_single_gpu(world, wname, overrides, exchange):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, wname, overrides, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, wname, overrides, exchange, q))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -1,0 +1,99 @@
+"""Expert-parallel peer exchange kernels, with G ranks emulated on one GPU.
+
+Every "rank" gets its own token, row-map and output buffers on the same device,
+and the address arrays the kernels take point at those buffers, so the device
+plan (``lr_ep_plan``), the owner-side gather (``lr_ep_gather``) and the
+token-side combine (``lr_ep_combine``) run exactly as across GPUs, one rank
+after the other (none of them waits on another rank).  The concatenated
+outputs must equal ``MoELayer.forward`` on the whole batch bit for bit, and the
+plan must equal a numpy restatement of the global slot-order capacity rule.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _plan_reference(counts: np.ndarray, rank: int, C: int) -> np.ndarray:
+    """numpy restatement of the plan layout documented in ``lr_ep_plan``."""
+    G, E = counts.shape
+    El = E // G
+    base = np.cumsum(counts, axis=0) - counts
+    kept = np.clip(C - base, 0, counts)
+    seg_start, seg_len = np.zeros(El, np.int64), np.zeros(El, np.int64)
+    row_base, src_off, kp = (np.zeros((El, G), np.int64) for _ in range(3))
+    row = 0
+    for el in range(El):
+        e = rank * El + el
+        seg_start[el] = row
+        for r in range(G):
+            row_base[el, r] = row + seg_len[el]
+            src_off[el, r] = counts[r, :e].sum()
+            kp[el, r] = kept[r, e]
+            seg_len[el] += kept[r, e]
+        row += seg_len[el]
+    my_off = np.cumsum(counts[rank]) - counts[rank]
+    my_kept = kept[rank]
+    dst_row = np.zeros(E, np.int64)
+    for e in range(E):
+        o, el = divmod(e, El)
+        dst_row[e] = kept[:, o * El:o * El + el].sum() + kept[:rank, e].sum()
+    return np.concatenate([seg_start, seg_len, row_base.ravel(), src_off.ravel(), kp.ravel(),
+                           my_off, my_kept, dst_row]).astype(np.int32)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("wname,overrides", [
+    ("prefill", dict(tokens=2048, d_model=1024, d_ff=2048)),
+    ("fine", dict(tokens=1024, d_model=512)),
+    ("decode", dict(tokens=64, d_model=1024, d_ff=2048)),
+])
+def test_peer_exchange_emulated_matches_single_gpu(world, wname, overrides):
+    from lightning_router import _ext
+    from lightning_router.kernels.expert_routing import expert_capacity
+    from lightning_router.workloads import WORKLOADS, build_layer
+    w = dataclasses.replace(WORKLOADS[wname], **overrides)
+    dev = torch.device("cuda", 0)
+    layer, t = build_layer(w, device=dev)
+    ops = _ext.ops()
+    err = _ext.error_word(0)
+    _ext.check_device_errors()
+    E, k, G = w.experts, w.top_k, world
+    El, T_l, d = E // G, w.tokens // G, w.d_model
+    C = expert_capacity(w.tokens * k, E, w.capacity_factor)
+    rows_max = El * C
+    ranks = []
+    for r in range(G):
+        x = t.x[r * T_l:(r + 1) * T_l].contiguous()
+        logits = layer.gate.logits(x)
+        ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = ops.topk_route(
+            logits, k, 1, float(layer.gate.load_balance_weight), err)
+        src = torch.zeros(T_l * k, dtype=torch.int32, device=dev)
+        ops.route_rows(ids, gw, offs, pos, ws, T_l, E, src)
+        ranks.append(dict(x=x, ids=ids, gw=gw, offs=offs, pos=pos, src=src,
+                          y=torch.empty(rows_max, d, dtype=torch.float16, device=dev),
+                          a=torch.empty(rows_max, d, dtype=torch.float16, device=dev)))
+    counts = torch.stack([(rk["offs"][1:] - rk["offs"][:-1]) for rk in ranks]).int().contiguous()
+    px = torch.tensor([rk["x"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    psrc = torch.tensor([rk["src"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    py = torch.tensor([rk["y"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    cnt_h = counts.cpu().numpy().astype(np.int64)
+    for r, rk in enumerate(ranks):
+        plan = ops.ep_plan(counts, r, C, err)
+        assert np.array_equal(plan.cpu().numpy(), _plan_reference(cnt_h, r, C))
+        a = ops.ep_gather(px, psrc, plan, E, r, T_l, T_l * k, d, rk["a"], err)
+        layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C, first_expert=r * El,
+                                       num_local=El, out=rk["y"])
+        rk["plan"] = plan
+    outs = [ops.ep_combine(py, rk["plan"], rk["ids"], rk["gw"], rk["pos"], T_l, E, rows_max, d,
+                           err) for rk in ranks]
+    _ext.check_device_errors()
+    full = torch.cat(outs)
+    ref, _ = layer(t.x)
+    assert torch.equal(full, ref), f"max |diff| {(full.float() - ref.float()).abs().max()}"
