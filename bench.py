@@ -6,7 +6,8 @@
 Default workload: the prefill layer (16384 tokens, d_model 4096, d_ff 14336,
 8 experts top-2, INT4 group-128 SwiGLU experts, capacity factor 1.25) on one GPU;
 with N > 1 ranks (torchrun) the experts are sharded expert-parallel, tokens are
-sharded by rank and exchanged with NCCL all-to-all (strong scaling: the 16384
+sharded by rank and exchanged over NVLink peer memory (``--exchange peer``, the
+default) or NCCL all-to-all (``--exchange nccl``) (strong scaling: the 16384
 tokens are split over the ranks).
 
 value     MoE-layer tokens/s of the whole job, device-timed (CUDA events, max over ranks),
@@ -240,7 +241,7 @@ def run_gpu(args, ws, rank, local):
     if ws > 1:
         from lightning_router.serving.ep import ExpertParallelMoE
         layer, t = build_layer(w, device=dev, gen_device=dev)
-        model = ExpertParallelMoE.from_layer(layer, ws, rank)
+        model = ExpertParallelMoE.from_layer(layer, ws, rank, exchange=args.exchange)
         T_local = w.tokens // ws
         x = t.x[rank * T_local:(rank + 1) * T_local].contiguous()
         del t
@@ -336,13 +337,19 @@ def run_gpu(args, ws, rank, local):
            "d2h_bytes_per_step": int(outh.numel() * 2) * ws,
            "api": "MoELayer.forward" if ws == 1 else "ExpertParallelMoE.forward"}
 
-    launches_per_step = 6
+    # gate, route, permute/route_rows, 2 GEMMs, combine; the peer exchange adds
+    # its plan and gather kernels
+    launches_per_step = 8 if (ws > 1 and args.exchange == "peer") else 6
+    if ws > 1:
+        barrier(ws)
+        model.close()
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": workload_desc(w), "global_batch": w.tokens, "seq_len": None,
                    "parallelism": parallel,
+                   **({"exchange": args.exchange} if ws > 1 else {}),
                    "l2": "inputs larger than L2 (INT4 weights "
                          f"{w.experts} experts, activations {w.tokens * w.d_model * 2 >> 20} MiB)"},
         "e2e": e2e,
@@ -452,6 +459,8 @@ def main():
                     help="override the token count (smaller profiling cases)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel token exchange (N > 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
