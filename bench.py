@@ -47,9 +47,14 @@ import torch  # noqa: E402
 METRIC = "MoE-layer tokens/s"
 UNIT = "tokens/s"
 
-# DRAM bytes per launch of the dominant kernel from ncu captures (profiles/*.md),
-# keyed by workload; None until captured.
-NCU_TRAFFIC = {}
+# DRAM bytes (read + write) per launch of the dominant kernel (the gate/up GEMM)
+# from full-size ncu captures of the bench's own timed steps, keyed by workload
+# (profiles/launches_prefill16k.md, profiles/launches_decode64.md); None until
+# captured.
+NCU_TRAFFIC = {
+    "prefill": 809.0e6 + 907.3e6,   # rows in 268 MB + weights 487 MB, rows out 940 MB
+    "decode": 489.8e6 + 2.6e6,      # weights 487 MB
+}
 
 
 def _peaks():
@@ -312,29 +317,28 @@ def run_gpu(args, ws, rank, local):
         "stage_ms": {k: round(v, 4) for k, v in st.items()},
     }
 
-    # end to end through the public API with host buffers (pinned), max over ranks
+    # end to end through the public API with host buffers (pinned), max over ranks: every
+    # step copies its input from pinned host memory and its output back, through the
+    # package's serving loop (copies on their own stream, overlapping the next / previous
+    # step's compute)
+    from lightning_router.serving.pipeline import HostPipeline
     xh = x.cpu().pin_memory()
-    outh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x)
-    for _ in range(max(1, args.warmup)):
-        xd.copy_(xh, non_blocking=True)
-        o, aux = fwd(xd)
-        outh.copy_(o, non_blocking=True)
+    outh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(fwd, x, dev)
+    pipe.run([xh] * max(1, args.warmup), [outh[i % 2] for i in range(max(1, args.warmup))])
     torch.cuda.synchronize()
     barrier(ws)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        xd.copy_(xh, non_blocking=True)
-        o, aux = fwd(xd)
-        outh.copy_(o, non_blocking=True)
+    pipe.run([xh] * args.steps, [outh[i % 2] for i in range(args.steps)])
     e1.record()
     torch.cuda.synchronize()
     barrier(ws)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws)
     e2e = {"value": w.tokens * args.steps / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": int(xh.numel() * 2) * ws,
-           "d2h_bytes_per_step": int(outh.numel() * 2) * ws,
+           "d2h_bytes_per_step": int(outh[0].numel() * 2) * ws,
+           "overlap": "host copies on a second stream, double-buffered (HostPipeline)",
            "api": "MoELayer.forward" if ws == 1 else "ExpertParallelMoE.forward"}
 
     # gate, route, permute/route_rows, 2 GEMMs, combine; the peer exchange adds

@@ -211,9 +211,13 @@ LR_DEVICE void build_tile_table(const int32_t* __restrict__ seg_start,
   if (lane == 0) s_tbase[E] = carry;
 }
 
-// tile -> (expert, token tile, feature tile)
+// tile -> (expert, token tile, feature tile).  Within an expert the token tiles
+// vary fastest (CTAs running at the same time share weight columns through L2),
+// or, with n_fastest, the feature tiles (they share token rows instead: better
+// when the expert's token rows outweigh its weights, e.g. a long-K down
+// projection).
 LR_DEVICE void decode_tile(const int* s_tbase, const int* s_mt, int E, int tile, int& e, int& mt,
-                           int& nt) {
+                           int& nt, bool n_fastest = false, int n_tiles = 1) {
   int lo = 0, hi = E;  // last e with s_tbase[e] <= tile
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -222,8 +226,13 @@ LR_DEVICE void decode_tile(const int* s_tbase, const int* s_mt, int E, int tile,
   }
   e = lo;
   const int local = tile - s_tbase[e];
-  nt = local / s_mt[e];
-  mt = local - nt * s_mt[e];
+  if (n_fastest) {
+    mt = local / n_tiles;
+    nt = local - mt * n_tiles;
+  } else {
+    nt = local / s_mt[e];
+    mt = local - nt * s_mt[e];
+  }
 }
 
 }  // namespace lr

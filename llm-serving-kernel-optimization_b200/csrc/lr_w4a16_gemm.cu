@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                               const ExpertEntry* __restrict__ table, int E, int mat, int K, int N,
                               const int32_t* __restrict__ seg_start,
                               const int32_t* __restrict__ seg_len, int max_rows, int R,
-                              __half* __restrict__ C, int32_t* err) {
+                              __half* __restrict__ C, int32_t* err, int n_fastest) {
   constexpr int STAGES = S::STAGES, DSTAGES = S::DSTAGES, DGROUPS = S::DGROUPS;
   constexpr int MT = S::MT, WN = S::WN, WJ = S::WJ, ROWS = S::ROWS;
   constexpr bool kGLU = MODE == LR_FFN_MODE_SWIGLU;
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   // tile -> (expert, token tile, feature tile); token tiles vary fastest
   auto decode = [&](int tile, int& e, int& mt, int& nt) {
-    decode_tile(s_tbase, s_mt, E, tile, e, mt, nt);
+    decode_tile(s_tbase, s_mt, E, tile, e, mt, nt, n_fastest != 0, n_tiles);
   };
 
   if (warp == kProdWarp) {
@@ -495,8 +495,12 @@ static int launch_gemm(const void* A, int K, int R, const ExpertEntry* table, in
   const long n_tiles = (N + BO - 1) / BO;
   const long upper = long(E) * ((max_rows + S::ROWS - 1) / S::ROWS) * n_tiles;
   const int grid = int(upper < sms ? (upper < 1 ? 1 : upper) : sms);
+  // token rows of an expert (max_rows x K fp16) against its weights (K x N / 2
+  // bytes, twice for SwiGLU): keep the larger one's tiles shared by concurrent CTAs
+  const long wcols = long(N) * (MODE == LR_FFN_MODE_SWIGLU ? 2 : 1);
+  const int n_fastest = long(max_rows) * 4 > wcols ? 1 : 0;
   kern<<<grid, kGemmThreads, S::kTotal, stream>>>(ta, table, E, mat, K, N, seg_start, seg_len,
-                                                  max_rows, R, C, err);
+                                                  max_rows, R, C, err, n_fastest);
   LR_LAUNCH_CHECK();
   return LR_OK;
 }
