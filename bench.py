@@ -236,6 +236,7 @@ def stage_times(events, steps):
 
 
 def run_gpu(args, ws, rank, local):
+    from lightning_router.kernels.expert_routing import SMALL_BATCH_TOKENS
     from lightning_router.workloads import WORKLOADS, build_layer
     w = WORKLOADS[args.workload]
     if args.tokens:
@@ -379,8 +380,12 @@ def run_gpu(args, ws, rank, local):
            "api": "MoELayer.forward" if ws == 1 else "ExpertParallelMoE.forward"}
 
     # gate, route, permute/route_rows, 2 GEMMs, combine; the peer exchange adds
-    # its plan and gather kernels
-    launches_per_step = 8 if (ws > 1 and args.exchange == "peer") else 6
+    # its plan and gather kernels; one GPU with at most 256 tokens runs the gate
+    # inside the route launch
+    if ws > 1:
+        launches_per_step = 8 if args.exchange == "peer" else 6
+    else:
+        launches_per_step = 5 if w.tokens <= SMALL_BATCH_TOKENS else 6
     if ws > 1:
         barrier(ws)
         model.close()

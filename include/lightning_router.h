@@ -77,6 +77,28 @@ int lr_topk_gating_dispatch(const void* x, const float* logits, int T, int d, in
                             int32_t* slot_pos, void* workspace, size_t workspace_bytes,
                             int32_t* err, lr_stream_t stream);
 
+/* Gate projection + lr_topk_gating_dispatch in one call (the reference's
+ * TopKGating.forward from hidden states, gating.py:48-101, then
+ * expert_routing_forward).  x[T,d] fp16 is both the gate input and the rows
+ * to permute; gate_weight[E,d] fp16, bias[E] fp32 (nullable); logits[T,E]
+ * fp32 receives the logits.  Other arguments and outputs as
+ * lr_topk_gating_dispatch.  For T <= 256 the projection, top-k, ranks,
+ * offsets and aux loss run in one launch and the row copy in a second; the
+ * logits are bit-identical to lr_gate_logits.  Larger T runs lr_gate_logits
+ * then lr_topk_gating_dispatch.  The workspace is
+ * lr_gate_dispatch_workspace_bytes(T, k, E).
+ * Limits: d % 16 == 0, E <= 64, 1 <= k <= min(E, 8); x, gate_weight and
+ * permuted 16-byte aligned.                                                */
+size_t lr_gate_dispatch_workspace_bytes(int num_tokens, int top_k, int num_experts);
+int lr_gate_topk_gating_dispatch(const void* x, const void* gate_weight, const float* bias, int T,
+                                 int d, int E, int k, int capacity, float load_balance_weight,
+                                 int fill_dropped, float* logits, int32_t* expert_ids,
+                                 float* gate_weights, int32_t* token_indices, int32_t* offsets,
+                                 int32_t* kept_counts, float* aux_loss, void* permuted,
+                                 float* routing_w, int32_t* source_idx, int32_t* slot_pos,
+                                 void* workspace, size_t workspace_bytes, int32_t* err,
+                                 lr_stream_t stream);
+
 /* The two phases of lr_topk_gating_dispatch, for expert-parallel callers that
  * exchange per-expert counts between them.
  * lr_topk_route: gating, slot ranks inside their 256-token route blocks (left in

@@ -17,6 +17,8 @@
 //             expert-wide rank < capacity.  Token rows are copied with 128-bit
 //             vector loads/stores; for gated routing each token row is read once
 //             and written to its k rows.
+// Small batches (T <= 256, decode) take the gate projection into the route
+// launch (gate_route_small_kernel) and copy the rows in a second one.
 #include "lr_common.cuh"
 
 namespace lr {
@@ -237,6 +239,71 @@ LR_DEVICE bool arrive_last(int32_t* ticket, int num_blocks, int* s_flag) {
 // ---------------------------------------------------------------------------
 // gating route: top-k softmax per token + slot ranks + histogram (+aux sums)
 // ---------------------------------------------------------------------------
+// One token's fp32 logits -> softmax probabilities p, the k experts with the
+// largest logits (descending, lowest index first on ties) and their weights
+// p / (sum of the selected p + 1e-9) (reference gating.py:69-85).
+template <int MAXE>
+LR_DEVICE void topk_softmax(const float (&l)[MAXE], int E, int k, float (&p)[MAXE],
+                            int (&ids)[kMaxTopK], float (&wsel)[kMaxTopK]) {
+  float m = l[0];
+#pragma unroll
+  for (int i = 1; i < MAXE; ++i)
+    if (i < E) m = fmaxf(m, l[i]);
+  float z = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXE; ++i) {
+    p[i] = (i < E) ? expf(l[i] - m) : 0.f;
+    z += p[i];
+  }
+#pragma unroll
+  for (int i = 0; i < MAXE; ++i) p[i] = (i < E) ? p[i] / z : 0.f;
+
+  uint64_t sel = 0;
+  float psel[kMaxTopK];
+  float ssum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    ids[j] = 0;
+    psel[j] = 0.f;
+    if (j < k) {
+      int best = -1;
+      float bv = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXE; ++i) {
+        if (i < E && !((sel >> i) & 1ull) && (best < 0 || l[i] > bv)) {
+          best = i;
+          bv = l[i];
+        }
+      }
+      sel |= 1ull << best;
+      ids[j] = best;
+      float pb = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXE; ++i)
+        if (i == best) pb = p[i];
+      psel[j] = pb;
+      ssum += pb;
+    }
+  }
+  const float denom = ssum + 1e-9f;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) wsel[j] = psel[j] / denom;
+}
+
+template <int MAXE>
+LR_DEVICE void warp_prob_sums(const float (&p)[MAXE], int E, float* s_pw) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < MAXE; ++i) {
+    if (i < E) {
+      float v = p[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) s_pw[warp * E + i] = v;
+    }
+  }
+}
+
 template <int MAXE>
 __global__ void __launch_bounds__(kRouteThreads)
     topk_route_kernel(const float* __restrict__ logits, int T, int E, int k, int C, float lbw,
@@ -253,7 +320,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   __shared__ int32_t s_tot[MAXE];
   __shared__ int s_last;
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int t = blockIdx.x * kRouteThreads + tid;
   const bool valid = t < T;
   const int ntok = min(kRouteThreads, T - int(blockIdx.x) * kRouteThreads);
@@ -266,47 +333,9 @@ __global__ void __launch_bounds__(kRouteThreads)
     const float* row = logits + size_t(valid ? t : 0) * E;
 #pragma unroll
     for (int i = 0; i < MAXE; ++i) l[i] = (i < E && valid) ? __ldg(row + i) : 0.f;
-    float m = l[0];
-#pragma unroll
-    for (int i = 1; i < MAXE; ++i)
-      if (i < E) m = fmaxf(m, l[i]);
-    float z = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXE; ++i) {
-      p[i] = (i < E) ? expf(l[i] - m) : 0.f;
-      z += p[i];
-    }
-#pragma unroll
-    for (int i = 0; i < MAXE; ++i) p[i] = (i < E) ? p[i] / z : 0.f;
-
-    // top-k on logits: descending, lowest index first on ties
-    uint64_t sel = 0;
     int ids[kMaxTopK];
-    float psel[kMaxTopK];
-    float ssum = 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j < k) {
-        int best = -1;
-        float bv = 0.f;
-#pragma unroll
-        for (int i = 0; i < MAXE; ++i) {
-          if (i < E && !((sel >> i) & 1ull) && (best < 0 || l[i] > bv)) {
-            best = i;
-            bv = l[i];
-          }
-        }
-        sel |= 1ull << best;
-        ids[j] = best;
-        float pb = 0.f;
-#pragma unroll
-        for (int i = 0; i < MAXE; ++i)
-          if (i == best) pb = p[i];
-        psel[j] = pb;
-        ssum += pb;
-      }
-    }
-    const float denom = ssum + 1e-9f;
+    float wsel[kMaxTopK];
+    topk_softmax<MAXE>(l, E, k, p, ids, wsel);
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
       if (j < k) {
@@ -314,7 +343,7 @@ __global__ void __launch_bounds__(kRouteThreads)
         if (valid) {
           const size_t s = size_t(t) * k + j;
           expert_ids[s] = ids[j];
-          gate_w[s] = psel[j] / denom;
+          gate_w[s] = wsel[j];
           if (token_idx) token_idx[s] = t;
         }
       }
@@ -326,17 +355,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   }
   // per-warp probability sums (aux loss)
   const bool want_p = aux_loss != nullptr || prob_sums != nullptr;
-  if (want_p) {
-#pragma unroll
-    for (int i = 0; i < MAXE; ++i) {
-      if (i < E) {
-        float v = p[i];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) s_pw[warp * E + i] = v;
-      }
-    }
-  }
+  if (want_p) warp_prob_sums<MAXE>(p, E, s_pw);
   __syncthreads();
 
   // slot ranks, chunk by chunk in slot order
@@ -406,6 +425,42 @@ __global__ void __launch_bounds__(kRouteThreads)
 // ---------------------------------------------------------------------------
 constexpr int kCopyUnroll = 8;
 
+// One warp copies 16-byte chunks [c_beg, c_end) of a token row to the rows of
+// its k slots.  Lane j < k holds slot j's destination row (`my_dst`, -1 for
+// none) and whether it is kept; a dropped slot's row is zero-filled iff `fill`.
+LR_DEVICE void copy_token_rows(const uint4* __restrict__ src, int c_beg, int c_end, int d8, int k,
+                               int my_dst, int my_kept, int fill, uint4* __restrict__ permuted) {
+  const int lane = threadIdx.x & 31;
+  int dst[kMaxTopK];
+  unsigned keptm = 0;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    dst[j] = __shfl_sync(0xffffffffu, my_dst, j);
+    keptm |= unsigned(__shfl_sync(0xffffffffu, my_kept, j) != 0) << j;
+  }
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int c0 = c_beg; c0 < c_end; c0 += 32 * kCopyUnroll) {
+    uint4 v[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < c_end) v[u] = ld_stream(src + c);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j < k && dst[j] >= 0 && (((keptm >> j) & 1u) || fill)) {
+        uint4* o = permuted + size_t(dst[j]) * d8;
+        const bool kj = (keptm >> j) & 1u;
+#pragma unroll
+        for (int u = 0; u < kCopyUnroll; ++u) {
+          const int c = c0 + u * 32 + lane;
+          if (c < c_end) o[c] = kj ? v[u] : zero;
+        }
+      }
+    }
+  }
+}
+
 // gated routing: one warp per token, the row is read once and written k times.
 // A slot's rank inside this shard's expert segment is blk_base + block rank;
 // its expert-wide rank adds rank_base[e] (the slots of lower shards, or 0).
@@ -437,35 +492,7 @@ __global__ void __launch_bounds__(256)
     slot_pos[s] = my_kept ? my_dst : -1;
   }
   if (permuted == nullptr) return;
-  int dst[kMaxTopK];
-  unsigned keptm = 0;
-#pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j) {
-    dst[j] = __shfl_sync(0xffffffffu, my_dst, j);
-    keptm |= unsigned(__shfl_sync(0xffffffffu, my_kept, j) != 0) << j;
-  }
-  const uint4* src = x + size_t(t) * d8;
-  const uint4 zero = make_uint4(0, 0, 0, 0);
-  for (int c0 = 0; c0 < d8; c0 += 32 * kCopyUnroll) {
-    uint4 v[kCopyUnroll];
-#pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) {
-      const int c = c0 + u * 32 + lane;
-      if (c < d8) v[u] = ld_stream(src + c);
-    }
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j < k && dst[j] >= 0 && (((keptm >> j) & 1u) || fill)) {
-        uint4* o = permuted + size_t(dst[j]) * d8;
-        const bool kj = (keptm >> j) & 1u;
-#pragma unroll
-        for (int u = 0; u < kCopyUnroll; ++u) {
-          const int c = c0 + u * 32 + lane;
-          if (c < d8) o[c] = kj ? v[u] : zero;
-        }
-      }
-    }
-  }
+  copy_token_rows(x + size_t(t) * d8, 0, d8, d8, k, my_dst, my_kept, fill, permuted);
 }
 
 // given slots: one warp per slot, row x[token_idx[s]] -> permuted[dst].
@@ -524,17 +551,265 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
-// combine: one warp per token, fp32 accumulation in slot order
+// small batches (decode): gate projection + top-k + ranks + rows in one launch
+// ---------------------------------------------------------------------------
+// For T <= 256 tokens a single block can rank every slot, so the route needs
+// no per-block bases.  The gate projection is spread over blocks by
+// (d-chunk c of kGateWarps, 16-token tile), warp w taking experts
+// [8w, 8w + 8): chunk c covers the k range of warp c of gate_logits_kernel
+// with the same mma.sync sequence per 8-expert group, and the last block to
+// finish sums the chunk partials in chunk order and adds the bias as that
+// kernel does, so the logits are bit-identical to the two-kernel path.
+// That block then runs top-k, ranks, CSR offsets, capacity and the aux loss for
+// all tokens and writes each slot's row; permute_rows_kernel copies the rows.
+constexpr int kSmallTokens = kRouteThreads;  // token limit of the one-block route
+constexpr int kSgTok = 16;                   // tokens per gate block (one mma tile)
+constexpr int kSgPiece = 512;                // k per shared-memory piece
+constexpr int kSgLd = kSgPiece + 8;          // padded row in halves: rows 4 banks apart
+
+struct SmallRouteWs {
+  int32_t* ticket;
+  float* part;        // [kGateWarps][T][E] partial logits
+  int32_t* slot_row;  // [T*k] row of each slot (dropped slots included)
+};
+
+static size_t small_route_ws_bytes(int T, int k, int E) {
+  return 256 + align256(size_t(kGateWarps) * T * E * sizeof(float)) +
+         align256(size_t(T) * k * sizeof(int32_t));
+}
+
+static SmallRouteWs carve_small_route_ws(void* ws, int T, int E) {
+  char* p = static_cast<char*>(ws);
+  SmallRouteWs r;
+  r.ticket = reinterpret_cast<int32_t*>(p);
+  p += 256;
+  r.part = reinterpret_cast<float*>(p);
+  p += align256(size_t(kGateWarps) * T * E * sizeof(float));
+  r.slot_row = reinterpret_cast<int32_t*>(p);
+  return r;
+}
+
+static size_t small_gate_smem_bytes(int E) {
+  return size_t(kSgTok + ((E + 7) & ~7)) * kSgLd * sizeof(__half);
+}
+
+// 16-byte global -> shared copy; with pred false the destination is zero-filled
+// and nothing is read.
+LR_DEVICE void cp_async16(uint32_t saddr, const void* gptr, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(gptr),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+LR_DEVICE void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+LR_DEVICE uint32_t lds_u32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+template <int MAXE>
+__global__ void __launch_bounds__(kRouteThreads)
+    gate_route_small_kernel(const __half* __restrict__ h, const __half* __restrict__ wg,
+                            const float* __restrict__ bias, int T, int d, int E, int k, int C,
+                            float lbw, float* __restrict__ logits,
+                            int32_t* __restrict__ expert_ids, float* __restrict__ gate_w,
+                            int32_t* __restrict__ token_idx, int32_t* __restrict__ offsets,
+                            int32_t* __restrict__ kept_counts, float* __restrict__ aux_loss,
+                            float* __restrict__ routing_w, int32_t* __restrict__ src_idx,
+                            int32_t* __restrict__ slot_pos, SmallRouteWs ws, int num_blocks) {
+  extern __shared__ __align__(16) __half s_gate[];  // [kSgTok][kSgLd] tokens, [Epad][kSgLd] gate
+  __shared__ int32_t s_ids[kRouteThreads * kMaxTopK];
+  __shared__ int32_t s_rank[kRouteThreads * kMaxTopK];
+  __shared__ int32_t s_wcnt[kWarps * MAXE];
+  __shared__ int32_t s_run[MAXE];
+  __shared__ int32_t s_off[MAXE];
+  __shared__ float s_pw[kWarps * MAXE];
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tq = lane & 3;
+
+  // ---- gate partials of d-chunk `chunk` for tokens [t0, t0 + 16)
+  {
+    const int chunk = blockIdx.x % kGateWarps;
+    const int t0 = (blockIdx.x / kGateWarps) * kSgTok;
+    const int kc = ((d / 16 + kGateWarps - 1) / kGateWarps) * 16;
+    const int kbeg = chunk * kc, kend = min(d, kbeg + kc);
+    const int epad = (E + 7) & ~7;
+    __half* s_h = s_gate;
+    __half* s_w = s_gate + kSgTok * kSgLd;
+    const int e0 = warp * 8;  // this warp's 8 experts
+    const bool active = e0 < E;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int p0 = kbeg; p0 < kend; p0 += kSgPiece) {
+      const int L = min(kSgPiece, kend - p0);  // a multiple of 16
+      const int cpr = L / 8;                    // 16-byte chunks per row
+      __syncthreads();                          // the previous piece is consumed
+      for (int i = tid; i < kSgTok * cpr; i += kRouteThreads) {
+        const int r = i / cpr, c = i - r * cpr;
+        const bool ok = t0 + r < T;
+        cp_async16(smem_u32(s_h + r * kSgLd + c * 8),
+                   h + size_t(ok ? t0 + r : 0) * d + p0 + c * 8, ok);
+      }
+      for (int i = tid; i < epad * cpr; i += kRouteThreads) {
+        const int r = i / cpr, c = i - r * cpr;
+        const bool ok = r < E;
+        cp_async16(smem_u32(s_w + r * kSgLd + c * 8), wg + size_t(ok ? r : 0) * d + p0 + c * 8,
+                   ok);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      if (active) {
+        const __half* a0 = s_h + g * kSgLd + 2 * tq;
+        const __half* a1 = a0 + 8 * kSgLd;
+        const __half* b = s_w + (e0 + g) * kSgLd + 2 * tq;
+#pragma unroll 4
+        for (int kk = 0; kk < L; kk += 16) {
+          uint32_t a[4];
+          a[0] = lds_u32(a0 + kk);
+          a[1] = lds_u32(a1 + kk);
+          a[2] = lds_u32(a0 + kk + 8);
+          a[3] = lds_u32(a1 + kk + 8);
+          mma_16816(acc, a, lds_u32(b + kk), lds_u32(b + kk + 8));
+        }
+      }
+    }
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = t0 + ((i < 2) ? g : g + 8);
+        const int col = e0 + 2 * tq + (i & 1);
+        if (row < T && col < E) ws.part[(size_t(chunk) * T + row) * E + col] = acc[i];
+      }
+    }
+  }
+  if (!arrive_last(ws.ticket, num_blocks, &s_last)) return;
+
+  // ---- last block: logits, top-k, ranks, offsets, rows (thread = token)
+  for (int i = tid; i < E; i += kRouteThreads) s_run[i] = 0;
+  const int t = tid;
+  const bool valid = t < T;
+  float p[MAXE];
+  int ids[kMaxTopK];
+  float wsel[kMaxTopK];
+  {
+    float l[MAXE];
+#pragma unroll
+    for (int i = 0; i < MAXE; ++i) {
+      float v = 0.f;
+      if (i < E && valid) {
+#pragma unroll
+        for (int c = 0; c < kGateWarps; ++c) v += __ldcg(ws.part + (size_t(c) * T + t) * E + i);
+        if (bias) v += __ldg(bias + i);
+        if (logits) logits[size_t(t) * E + i] = v;
+      }
+      l[i] = v;
+    }
+    topk_softmax<MAXE>(l, E, k, p, ids, wsel);
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j < k) {
+      s_ids[tid * k + j] = ids[j];
+      if (valid) {
+        const size_t s = size_t(t) * k + j;
+        expert_ids[s] = ids[j];
+        gate_w[s] = wsel[j];
+        if (token_idx) token_idx[s] = t;
+      }
+    }
+  }
+  if (!valid) {
+#pragma unroll
+    for (int i = 0; i < MAXE; ++i) p[i] = 0.f;
+  }
+  if (aux_loss) warp_prob_sums<MAXE>(p, E, s_pw);
+  __syncthreads();
+  const int nslots = T * k;
+  for (int c = 0; c < k; ++c) {
+    const int ls = c * kRouteThreads + tid;
+    const bool sv = ls < nslots;
+    const int r = rank_chunk(sv ? s_ids[ls] : -1, sv, E, s_wcnt, s_run);
+    if (sv) s_rank[ls] = r;
+  }
+  // s_run[e] now counts expert e's slots (uncapped)
+  if (tid == 0) {
+    int run = 0;
+    double aux = 0.0;
+    offsets[0] = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = run;
+      run += s_run[e];
+      offsets[e + 1] = run;
+      if (kept_counts) kept_counts[e] = min(s_run[e], C);
+      if (aux_loss) {
+        double P = 0.0;
+        for (int w = 0; w < kWarps; ++w) P += double(s_pw[w * E + e]);
+        aux += (double(s_run[e]) / double(nslots)) * (P / double(T));
+      }
+    }
+    if (aux_loss) aux_loss[0] = static_cast<float>(double(lbw) * double(E) * aux);
+    *ws.ticket = 0;
+  }
+  __syncthreads();
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j < k) {
+        const int s = t * k + j;
+        const int r = s_rank[tid * k + j];
+        const bool kept = r < C;
+        const int dst = s_off[ids[j]] + r;
+        routing_w[dst] = kept ? wsel[j] : 0.f;
+        src_idx[dst] = t;
+        slot_pos[s] = kept ? dst : -1;
+        ws.slot_row[s] = dst;
+      }
+    }
+  }
+}
+
+// Row copy after gate_route_small_kernel: one warp per (token, 1/parts of the row).
+__global__ void __launch_bounds__(256)
+    permute_rows_kernel(const uint4* __restrict__ x, int T, int d8, int k, int parts, int fill,
+                        const int32_t* __restrict__ slot_pos,
+                        const int32_t* __restrict__ slot_row, uint4* __restrict__ permuted) {
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int t = gw / parts, part = gw % parts;
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  int my_dst = -1, my_kept = 0;
+  if (lane < k) {
+    const size_t s = size_t(t) * k + lane;
+    my_dst = __ldg(slot_row + s);
+    my_kept = __ldg(slot_pos + s) >= 0;
+  }
+  const int seg = (d8 + parts - 1) / parts;
+  const int c_beg = part * seg, c_end = min(d8, c_beg + seg);
+  copy_token_rows(x + size_t(t) * d8, c_beg, c_end, d8, k, my_dst, my_kept, fill, permuted);
+}
+
+// ---------------------------------------------------------------------------
+// combine: one warp per (token, 1/parts of the row), fp32 accumulation in
+// slot order (the split only spreads small batches over more warps)
 // ---------------------------------------------------------------------------
 constexpr int kCombUnroll = 4;
 
+// Row parts per token: enough warps in flight for small batches, each part
+// at least 64 16-byte chunks.
+static int row_parts(long T, int d8) {
+  int parts = 1;
+  while (parts < 8 && T * parts < 2048 && d8 / (parts * 2) >= 64) parts *= 2;
+  return parts;
+}
+
 __global__ void __launch_bounds__(256)
     combine_kernel(const uint4* __restrict__ y, const float* __restrict__ gate_w,
-                   const int32_t* __restrict__ slot_pos, int T, int k, int d8,
+                   const int32_t* __restrict__ slot_pos, int T, int k, int d8, int parts,
                    uint4* __restrict__ out) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int t = gw / parts, part = gw % parts;
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
+  const int seg = (d8 + parts - 1) / parts;
+  const int c_beg = part * seg, c_end = min(d8, c_beg + seg);
   int my_pos = -1;
   float my_w = 0.f;
   if (lane < k) {
@@ -548,7 +823,7 @@ __global__ void __launch_bounds__(256)
     pos[j] = __shfl_sync(0xffffffffu, my_pos, j);
     w[j] = __shfl_sync(0xffffffffu, my_w, j);
   }
-  for (int c0 = 0; c0 < d8; c0 += 32 * kCombUnroll) {
+  for (int c0 = c_beg; c0 < c_end; c0 += 32 * kCombUnroll) {
     float acc[kCombUnroll][8];
 #pragma unroll
     for (int u = 0; u < kCombUnroll; ++u)
@@ -562,19 +837,19 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int u = 0; u < kCombUnroll; ++u) {
           const int c = c0 + u * 32 + lane;
-          if (c < d8) v[u] = ld_stream(row + c);
+          if (c < c_end) v[u] = ld_stream(row + c);
         }
 #pragma unroll
         for (int u = 0; u < kCombUnroll; ++u) {
           const int c = c0 + u * 32 + lane;
-          if (c < d8) acc_half8(acc[u], v[u], w[j]);
+          if (c < c_end) acc_half8(acc[u], v[u], w[j]);
         }
       }
     }
 #pragma unroll
     for (int u = 0; u < kCombUnroll; ++u) {
       const int c = c0 + u * 32 + lane;
-      if (c < d8) out[size_t(t) * d8 + c] = pack_half8(acc[u]);
+      if (c < c_end) out[size_t(t) * d8 + c] = pack_half8(acc[u]);
     }
   }
 }
@@ -796,6 +1071,83 @@ extern "C" int lr_topk_gating_dispatch(const void* x, const float* logits, int T
                            workspace_bytes, stream);
 }
 
+extern "C" size_t lr_gate_dispatch_workspace_bytes(int num_tokens, int top_k, int num_experts) {
+  const size_t big = lr_route_workspace_bytes(num_tokens, top_k, num_experts);
+  if (num_tokens < 1 || num_tokens > kSmallTokens || top_k < 1 || num_experts < 1) return big;
+  const size_t small = small_route_ws_bytes(num_tokens, top_k, num_experts);
+  return small > big ? small : big;
+}
+
+template <int MAXE>
+static int launch_gate_route_small(const void* x, const void* wg, const float* bias, int T, int d,
+                                   int E, int k, int capacity, float lbw, float* logits,
+                                   int32_t* expert_ids, float* gate_weights,
+                                   int32_t* token_indices, int32_t* offsets,
+                                   int32_t* kept_counts, float* aux_loss, float* routing_w,
+                                   int32_t* source_idx, int32_t* slot_pos, SmallRouteWs ws,
+                                   cudaStream_t stream) {
+  auto kern = gate_route_small_kernel<MAXE>;
+  static unsigned long long configured = 0;
+  if (const int rc = set_dyn_smem_once(kern, int(small_gate_smem_bytes(64)), configured)) return rc;
+  const int blocks = kGateWarps * ((T + kSgTok - 1) / kSgTok);
+  kern<<<blocks, kRouteThreads, small_gate_smem_bytes(E), stream>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(wg), bias, T, d, E, k, capacity,
+      lbw, logits, expert_ids, gate_weights, token_indices, offsets, kept_counts, aux_loss,
+      routing_w, source_idx, slot_pos, ws, blocks);
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
+extern "C" int lr_gate_topk_gating_dispatch(
+    const void* x, const void* gate_weight, const float* bias, int T, int d, int E, int k,
+    int capacity, float load_balance_weight, int fill_dropped, float* logits,
+    int32_t* expert_ids, float* gate_weights, int32_t* token_indices, int32_t* offsets,
+    int32_t* kept_counts, float* aux_loss, void* permuted, float* routing_w, int32_t* source_idx,
+    int32_t* slot_pos, void* workspace, size_t workspace_bytes, int32_t* err,
+    lr_stream_t stream) {
+  if (T <= 0 || d <= 0 || d % 16 != 0 || E < 1 || E > 64 || k < 1 || k > kMaxTopK || k > E ||
+      capacity < 1)
+    return LR_ERR_INVALID_ARGUMENT;
+  if (!x || !gate_weight || !logits || !expert_ids || !gate_weights || !offsets || !routing_w ||
+      !source_idx || !slot_pos)
+    return LR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(gate_weight) || (permuted && !aligned16(permuted)))
+    return LR_ERR_INVALID_ARGUMENT;
+  if (T > kSmallTokens) {
+    const int rc = lr_gate_logits(x, gate_weight, bias, T, d, E, logits, stream);
+    if (rc != LR_OK) return rc;
+    return lr_topk_gating_dispatch(x, logits, T, d, E, k, capacity, load_balance_weight,
+                                   fill_dropped, expert_ids, gate_weights, token_indices, offsets,
+                                   kept_counts, aux_loss, permuted, routing_w, source_idx,
+                                   slot_pos, workspace, workspace_bytes, err, stream);
+  }
+  if (!workspace || workspace_bytes < small_route_ws_bytes(T, k, E)) return LR_ERR_WORKSPACE;
+  SmallRouteWs ws = carve_small_route_ws(workspace, T, E);
+  LR_CUDA_TRY(cudaMemsetAsync(ws.ticket, 0, sizeof(int32_t), stream));
+  int rc;
+#define LR_SMALL_CASE(ME)                                                                       \
+  rc = launch_gate_route_small<ME>(x, gate_weight, bias, T, d, E, k, capacity,                  \
+                                   load_balance_weight, logits, expert_ids, gate_weights,       \
+                                   token_indices, offsets, kept_counts, aux_loss, routing_w,    \
+                                   source_idx, slot_pos, ws, stream)
+  if (E <= 8)
+    LR_SMALL_CASE(8);
+  else if (E <= 16)
+    LR_SMALL_CASE(16);
+  else if (E <= 32)
+    LR_SMALL_CASE(32);
+  else
+    LR_SMALL_CASE(64);
+#undef LR_SMALL_CASE
+  if (rc != LR_OK || permuted == nullptr) return rc;
+  const int parts = row_parts(T, d / 8);
+  permute_rows_kernel<<<unsigned((long(T) * parts + 7) / 8), 256, 0, stream>>>(
+      static_cast<const uint4*>(x), T, d / 8, k, parts, fill_dropped, slot_pos, ws.slot_row,
+      static_cast<uint4*>(permuted));
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
 extern "C" size_t lr_dispatch_workspace_bytes(int num_slots, int num_experts) {
   const int B = (num_slots + kSlotBlock - 1) / kSlotBlock;
   return route_ws_bytes_for(B < 1 ? 1 : B, num_experts, false);
@@ -845,8 +1197,10 @@ extern "C" int lr_combine(const void* y, const float* gate_weights, const int32_
   if (T == 0) return LR_OK;
   if (!y || !gate_weights || !slot_pos || !out || !aligned16(y) || !aligned16(out))
     return LR_ERR_INVALID_ARGUMENT;
-  combine_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const uint4*>(y), gate_weights,
-                                                  slot_pos, T, k, d / 8, static_cast<uint4*>(out));
+  const int parts = row_parts(T, d / 8);
+  combine_kernel<<<unsigned((long(T) * parts + 7) / 8), 256, 0, stream>>>(
+      static_cast<const uint4*>(y), gate_weights, slot_pos, T, k, d / 8, parts,
+      static_cast<uint4*>(out));
   LR_LAUNCH_CHECK();
   return LR_OK;
 }

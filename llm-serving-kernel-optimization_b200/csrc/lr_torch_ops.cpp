@@ -109,6 +109,51 @@ std::vector<at::Tensor> topk_gating_dispatch(const c10::optional<at::Tensor>& x,
   return {ids, gw, tok, offsets, kept, aux, permuted, rw, src, pos};
 }
 
+// Gate projection + gating dispatch; returns {logits, then topk_gating_dispatch's outputs}.
+std::vector<at::Tensor> gate_topk_gating_dispatch(const at::Tensor& x, const at::Tensor& wg,
+                                                  const c10::optional<at::Tensor>& bias,
+                                                  int64_t k, int64_t capacity, double lbw,
+                                                  bool fill_dropped, bool permute,
+                                                  const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  check_cuda(wg, "wg");
+  TORCH_CHECK(x.dim() == 2 && wg.dim() == 2 && x.size(1) == wg.size(1), "x (T,d), wg (E,d)");
+  TORCH_CHECK(x.scalar_type() == at::kHalf && wg.scalar_type() == at::kHalf,
+              "gate_topk_gating_dispatch: fp16 x and wg expected");
+  const float* b = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    check_cuda(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == wg.size(0), "bias");
+    b = bias->data_ptr<float>();
+  }
+  const int64_t T = x.size(0), d = x.size(1), E = wg.size(0), S = T * k;
+  c10::cuda::CUDAGuard g(x.device());
+  auto iopt = x.options().dtype(at::kInt);
+  auto fopt = x.options().dtype(at::kFloat);
+  auto logits = at::empty({T, E}, fopt);
+  auto ids = at::empty({S}, iopt);
+  auto gw = at::empty({S}, fopt);
+  auto tok = at::empty({S}, iopt);
+  auto offsets = at::empty({E + 1}, iopt);
+  auto kept = at::empty({E}, iopt);
+  auto aux = at::empty({}, fopt);
+  auto rw = at::empty({S}, fopt);
+  auto src = at::empty({S}, iopt);
+  auto pos = at::empty({S}, iopt);
+  auto permuted = permute ? at::empty({S, d}, x.options()) : at::empty({0}, x.options());
+  auto ws = workspace(lr_gate_dispatch_workspace_bytes(int(T), int(k), int(E)), x);
+  check_status(lr_gate_topk_gating_dispatch(
+                   x.data_ptr(), wg.data_ptr(), b, int(T), int(d), int(E), int(k), int(capacity),
+                   float(lbw), fill_dropped ? 1 : 0, logits.data_ptr<float>(),
+                   ids.data_ptr<int32_t>(), gw.data_ptr<float>(), tok.data_ptr<int32_t>(),
+                   offsets.data_ptr<int32_t>(), kept.data_ptr<int32_t>(), aux.data_ptr<float>(),
+                   permute ? permuted.data_ptr() : nullptr, rw.data_ptr<float>(),
+                   src.data_ptr<int32_t>(), pos.data_ptr<int32_t>(), ws.data_ptr(),
+                   size_t(ws.numel()), err_ptr(err), cur_stream()),
+               "gate_topk_gating_dispatch");
+  return {logits, ids, gw, tok, offsets, kept, aux, permuted, rw, src, pos};
+}
+
 // Phase 1 of the fused dispatch; the returned workspace must be passed to permute_tokens.
 std::vector<at::Tensor> topk_route(const at::Tensor& logits, int64_t k, int64_t capacity,
                                    double lbw, const c10::optional<at::Tensor>& err) {
@@ -424,6 +469,9 @@ TORCH_LIBRARY(lightning_router, m) {
       "topk_gating_dispatch(Tensor? x, Tensor logits, int k, int capacity, float lbw, "
       "bool fill_dropped, bool with_aux, Tensor? err) -> Tensor[]");
   m.def(
+      "gate_topk_gating_dispatch(Tensor x, Tensor wg, Tensor? bias, int k, int capacity, "
+      "float lbw, bool fill_dropped, bool permute, Tensor? err) -> Tensor[]");
+  m.def(
       "expert_routing_forward(Tensor tokens, Tensor expert_ids, Tensor gate_weights, "
       "Tensor token_indices, int num_experts, int capacity, bool fill_dropped, Tensor? err) -> "
       "Tensor[]");
@@ -459,6 +507,7 @@ TORCH_LIBRARY(lightning_router, m) {
 TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
   m.impl("gate_logits", &gate_logits);
   m.impl("topk_gating_dispatch", &topk_gating_dispatch);
+  m.impl("gate_topk_gating_dispatch", &gate_topk_gating_dispatch);
   m.impl("expert_routing_forward", &expert_routing_forward);
   m.impl("combine", &combine);
   m.impl("topk_route", &topk_route);

@@ -479,11 +479,8 @@ static int launch_gemm(const void* A, int K, int R, const ExpertEntry* table, in
                        int N, const int32_t* seg_start, const int32_t* seg_len, int max_rows,
                        __half* C, int32_t* err, cudaStream_t stream) {
   auto kern = w4a16_grouped_gemm_kernel<S, MODE>;
-  static int configured = 0;
-  if (!configured) {
-    LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal));
-    configured = 1;
-  }
+  static unsigned long long configured = 0;
+  if (const int rc = set_dyn_smem_once(kern, S::kTotal, configured)) return rc;
   CUtensorMap ta;
   const int rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
                            uint64_t(K) * 2, kBK, uint32_t(S::ROWS), CU_TENSOR_MAP_SWIZZLE_128B);

@@ -24,6 +24,7 @@ C_ABI_SYMBOLS = (
     "lr_status_string", "lr_abi_version", "lr_last_cuda_error",
     "lr_gate_logits",
     "lr_route_workspace_bytes", "lr_topk_gating_dispatch", "lr_topk_gating_dispatch_noalloc",
+    "lr_gate_dispatch_workspace_bytes", "lr_gate_topk_gating_dispatch",
     "lr_topk_route", "lr_permute_tokens",
     "lr_dispatch_workspace_bytes", "lr_expert_routing_forward",
     "lr_combine", "lr_gather_workspace_bytes", "lr_expert_routing_gather",
@@ -52,6 +53,7 @@ def clib() -> ctypes.CDLL:
     lib.lr_status_string.restype = ctypes.c_char_p
     lib.lr_status_string.argtypes = [ctypes.c_int]
     for name in ("lr_route_workspace_bytes", "lr_dispatch_workspace_bytes",
+                 "lr_gate_dispatch_workspace_bytes",
                  "lr_gather_workspace_bytes", "lr_weight_table_bytes",
                  "lr_grouped_gemm_workspace_bytes"):
         getattr(lib, name).restype = ctypes.c_size_t

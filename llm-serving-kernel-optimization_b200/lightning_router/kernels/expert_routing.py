@@ -13,9 +13,12 @@ Drop-in for the reference's ``lightning_router/kernels/expert_routing.py``:
 * :func:`expert_routing_gather` (reference ``:274-298``) -- weighted return to
   token order, fp32 accumulation in ascending row order, one fp16 store (the
   reference accumulates with fp16 atomics in arbitrary order).
-* :func:`topk_gating_dispatch` -- the fused path used by ``MoELayer``: top-k
-  softmax gating from fp32 logits, histogram, scan, capacity and permutation in
-  two kernel launches with no host synchronisation.
+* :func:`topk_gating_dispatch` -- top-k softmax gating from fp32 logits,
+  histogram, scan, capacity and permutation in two kernel launches with no host
+  synchronisation.
+* :func:`gate_topk_gating_dispatch` -- the path used by ``MoELayer``: the gate
+  projection followed by the above; up to 256 tokens (decode) the projection
+  joins the routing launch.
 * :func:`combine` -- token-major weighted combine driven by ``slot_pos``.
 
 Slot ``s = t * k + j`` lists token ``t``'s experts in descending logit order,
@@ -29,6 +32,10 @@ from typing import NamedTuple
 import torch
 
 from lightning_router import _ext
+
+
+# token count up to which the gate projection runs inside the routing launch
+SMALL_BATCH_TOKENS = 256
 
 
 def expert_capacity(num_slots: int, num_experts: int, capacity_factor: float) -> int:
@@ -66,6 +73,30 @@ def topk_gating_dispatch(x: torch.Tensor | None, logits: torch.Tensor, top_k: in
         None if x is None else x.contiguous(), logits.contiguous().float(), int(top_k), C,
         float(load_balance_weight), bool(fill_dropped), True, err)
     return RoutingPlan(*outs, capacity=C)
+
+
+def gate_topk_gating_dispatch(x: torch.Tensor, gate_weight: torch.Tensor,
+                              bias: torch.Tensor | None, top_k: int,
+                              capacity_factor: float = 1.25, load_balance_weight: float = 0.01,
+                              fill_dropped: bool = False, capacity: int | None = None,
+                              permute: bool = True) -> tuple[torch.Tensor, RoutingPlan]:
+    """Gate projection ``x @ gate_weight.T (+ bias)`` followed by
+    :func:`topk_gating_dispatch`; returns ``(logits, plan)``.
+
+    ``x`` (T, d) fp16 is the gate input and the rows to permute (``permute=False``:
+    routing metadata only); ``gate_weight`` (E, d) fp16.  Up to 256 tokens the
+    projection, top-k and routing run in one kernel launch (plus the row copy);
+    the logits are bit-identical to :func:`gate_logits` either way.
+    """
+    _ext.require_cuda(x, gate_weight)
+    T, E = x.shape[0], gate_weight.shape[0]
+    C = expert_capacity(T * top_k, E, capacity_factor) if capacity is None else int(capacity)
+    err = _ext.error_word(x.device.index)
+    outs = _ext.ops().gate_topk_gating_dispatch(
+        x.half().contiguous(), gate_weight.half().contiguous(),
+        None if bias is None else bias.float().contiguous(), int(top_k), C,
+        float(load_balance_weight), bool(fill_dropped), bool(permute), err)
+    return outs[0], RoutingPlan(*outs[1:], capacity=C)
 
 
 def expert_routing_forward(

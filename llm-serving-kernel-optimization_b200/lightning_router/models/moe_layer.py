@@ -6,6 +6,7 @@ launches and no host synchronisation:
 
 1. gate projection             fp16 h . fp16 Wg^T -> fp32 logits        (CUDA cores / mma.sync)
 2. top-k softmax + histogram   ids, weights, slot ranks, aux loss, CSR offsets
+   (up to 256 tokens, 1 and 2 are one launch: the decode step is five)
 3. permute                     token rows -> expert-contiguous rows (kept slots only)
 4. grouped W4A16 gate/up GEMM  tcgen05, fused SwiGLU (or SiLU) epilogue
 5. grouped W4A16 down GEMM     tcgen05
@@ -24,7 +25,8 @@ import torch.nn as nn
 
 from lightning_router.config import KernelConfig, ModelConfig, MoEConfig, QuantizationConfig
 from lightning_router.kernels.expert_routing import (
-    RoutingPlan, combine, expert_capacity, topk_gating_dispatch)
+    SMALL_BATCH_TOKENS, RoutingPlan, combine, expert_capacity, gate_topk_gating_dispatch,
+    topk_gating_dispatch)
 from lightning_router.models.experts import ExpertGroup
 from lightning_router.models.gating import TopKGating
 
@@ -70,6 +72,14 @@ class MoELayer(nn.Module):
 
     def route(self, hidden_states: torch.Tensor) -> tuple[torch.Tensor, RoutingPlan]:
         """Gate logits and the dispatch plan (rows permuted) for (T, d) fp16 input."""
+        if hidden_states.shape[0] <= SMALL_BATCH_TOKENS:
+            # decode-sized batches: projection, top-k and routing in one launch
+            logits, plan = gate_topk_gating_dispatch(
+                hidden_states, self.gate.gate_proj.weight.detach(), self.gate.logit_bias,
+                self.top_k, load_balance_weight=self.gate.load_balance_weight,
+                capacity=self.capacity(hidden_states.shape[0]))
+            self._mark("gate")
+            return logits, plan
         logits = self.gate.logits(hidden_states)
         self._mark("gate")
         plan = topk_gating_dispatch(hidden_states, logits, self.top_k,

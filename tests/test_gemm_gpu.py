@@ -207,3 +207,38 @@ def test_grouped_repeat_is_bit_identical(mode, lens, maxr):
     ref = x @ deq[0][1].float() if mode == 0 else \
         torch.nn.functional.silu(x @ deq[0][0].float()) * (x @ deq[0][1].float())
     _check(outs[0][st:st + L], ref)
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+@pytest.mark.parametrize("lens", [[20, 7, 31, 12, 1, 30, 0, 25], [50, 7, 64, 12, 1, 30, 0, 25]])
+def test_expert_rows_independent_of_other_experts(mode, lens):
+    """An expert's output rows are bit-identical whether it runs alone or among 8
+    experts (other tile counts, tile order and SM assignment): every output
+    element keeps the same k-ordered UMMA accumulation.  Expert-parallel ranks
+    rely on this to match one GPU bit for bit."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16, weight_table
+    E, d, f, g = 8, 256, 4096, 64
+    q, s, z, deq = [], [], [], []
+    for e in range(E):
+        for m, (K, N) in enumerate([(d, f), (d, f), (f, d)]):
+            qw, sc, zr, Wd = _quant(K, N, g, 500 + e * 3 + m)
+            q.append(qw), s.append(sc), z.append(zr)
+            if e == 0:
+                deq.append(Wd)
+    starts = [0]
+    for L in lens[:-1]:
+        starts.append(starts[-1] + L)
+    R = starts[-1] + lens[-1]
+    A = torch.randn(R, d, generator=torch.Generator().manual_seed(3)).half().to(DEV)
+    ss = torch.tensor(starts, dtype=torch.int32, device=DEV)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    table8 = weight_table(q, s, z, E, d, f, g, True)
+    table1 = weight_table(q[:3], s[:3], z[:3], 1, d, f, g, True)
+    L0 = lens[0]
+    out8 = grouped_w4a16(table8, E, mode, 1, A, f, ss, sl, max(lens))
+    out1 = grouped_w4a16(table1, 1, mode, 1, A, f, ss[:1], sl[:1], L0)
+    assert torch.equal(out8[:L0], out1[:L0])
+    x = A[:L0].float()
+    ref = x @ deq[1].float() if mode == 0 else \
+        torch.nn.functional.silu(x @ deq[0].float()) * (x @ deq[1].float())
+    _check(out1[:L0], ref)

@@ -279,3 +279,64 @@ def test_dispatch_sweep_full_size_properties(T, cf):
     wk = torch.where(plan.slot_pos >= 0, plan.gate_weights, torch.zeros_like(plan.gate_weights))
     ref = (x.float() * wk.view(T, 2).sum(1, keepdim=True))
     torch.testing.assert_close(out.float(), ref, rtol=2e-3, atol=2e-3)
+
+
+GATE_DISPATCH_CASES = [
+    # T, d, E, k, cf, bias, fill
+    (64, 4096, 8, 2, 1.25, False, False),     # decode layer shape
+    (1, 64, 4, 1, 1.0, False, True),
+    (37, 256, 64, 6, 1.5, True, True),
+    (256, 1024, 33, 8, 0.5, True, False),     # the one-block limit, heavy drops
+    (200, 8192, 16, 2, 1.0, False, True),     # two shared-memory pieces per d-chunk
+    (130, 16, 8, 2, 1.0, True, True),         # d smaller than the 8 chunks
+    (257, 512, 8, 2, 1.25, False, True),      # just above the limit: two-kernel path
+    (1000, 256, 64, 6, 1.5, True, False),
+]
+
+
+@pytest.mark.parametrize("T,d,E,k,cf,use_bias,fill", GATE_DISPATCH_CASES)
+def test_gate_topk_dispatch_equals_two_kernel_path(T, d, E, k, cf, use_bias, fill):
+    """Gate projection + dispatch in one call: logits bit-identical to gate_logits,
+    every plan output identical to topk_gating_dispatch on those logits, and the
+    routing bit-exact against the oracle."""
+    from lightning_router.kernels.expert_routing import (
+        gate_logits, gate_topk_gating_dispatch, topk_gating_dispatch)
+    g = torch.Generator().manual_seed(T * 7 + E)
+    x = torch.randn(T, d, generator=g).half().to(DEV)
+    wg = (torch.randn(E, d, generator=g) * 0.05).half().to(DEV)
+    bias = torch.randn(E, generator=g).to(DEV) if use_bias else None
+    logits, plan = gate_topk_gating_dispatch(x, wg, bias, k, cf, fill_dropped=fill)
+    ref_logits = gate_logits(x, wg, bias)
+    assert torch.equal(logits, ref_logits)
+    ref = topk_gating_dispatch(x, ref_logits, k, cf, fill_dropped=fill)
+    for name in ("expert_ids", "gate_weights", "token_indices", "offsets", "kept_counts",
+                 "routing_weights", "source_indices", "slot_pos"):
+        assert torch.equal(getattr(plan, name), getattr(ref, name)), name
+    assert torch.equal(plan.aux_loss, ref.aux_loss)
+    kept = plan.slot_pos >= 0
+    rows = plan.slot_pos[kept].long()
+    assert torch.equal(plan.permuted[rows], ref.permuted[rows])
+    if fill:
+        assert torch.equal(plan.permuted, ref.permuted)
+    check_plan(plan, x.cpu(), logits.cpu(), k, cf, fill=fill)
+    # routing metadata only
+    logits2, plan2 = gate_topk_gating_dispatch(x, wg, bias, k, cf, permute=False)
+    assert torch.equal(logits2, logits) and plan2.permuted.numel() == 0
+    assert torch.equal(plan2.slot_pos, plan.slot_pos)
+
+
+def test_combine_small_batch_split_rows_bit_identical():
+    """Small batches spread each token's row over several warps; every output
+    element keeps its slot-order fp32 accumulation, so the result equals the
+    one-warp-per-token combine of a large batch holding the same tokens."""
+    from lightning_router.kernels.expert_routing import combine, topk_gating_dispatch
+    T, d, E, k, reps = 64, 4096, 8, 2, 40
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(T, d, generator=g).half().to(DEV)
+    logits = torch.randn(T, E, generator=g).to(DEV)
+    plan = topk_gating_dispatch(x, logits, k, 1.0)
+    y = torch.randn(T * k, d, generator=g).half().to(DEV)
+    small = combine(y, plan.gate_weights, plan.slot_pos, T, k)
+    big = combine(y, plan.gate_weights.repeat(reps), plan.slot_pos.repeat(reps), T * reps, k)
+    assert torch.equal(big[:T], small)
+    assert torch.equal(big[T * (reps - 1):], small)
