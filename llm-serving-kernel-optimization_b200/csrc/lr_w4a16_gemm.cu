@@ -26,8 +26,12 @@
 //               int32 words (TMA-staged) + per-group scale / zero (read from
 //               global memory) -> fp16(scale * (q - zero)), written into the
 //               128-byte-swizzled MN-major operand buffer of their k-step
-//   warp 16     producer: TMA loads of the token box and the packed weight box(es)
-//   warp 17     TMEM allocation + single-thread tcgen05.mma issue
+//   warp 16     token producer: TMA loads of the token box into the token ring,
+//               whose stages the MMA releases (tcgen05.commit)
+//   warp 17     weight producer: TMA loads of the packed weight box(es) into the
+//               weight ring, whose stages the dequant warps release as soon as
+//               they have read the words, so weights run ahead of the MMA
+//   warp 18     TMEM allocation + single-thread tcgen05.mma issue
 //
 // Every mbarrier wait is bounded in time; a wait that runs out raises a
 // shared abort flag and LR_DEVERR_PIPE_TIMEOUT so all roles drain and exit.
@@ -39,8 +43,9 @@ namespace lr {
 
 constexpr int kEpiWarps = 8;
 constexpr int kDeqWarps = 8;
-constexpr int kProdWarp = kEpiWarps + kDeqWarps;
-constexpr int kMmaWarp = kProdWarp + 1;
+constexpr int kProdWarp = kEpiWarps + kDeqWarps;  // token ring
+constexpr int kWProdWarp = kProdWarp + 1;         // packed-weight ring
+constexpr int kMmaWarp = kWProdWarp + 1;
 constexpr int kGemmThreads = (kMmaWarp + 1) * 32;
 
 // Tile shape: MT sub-tiles of 128 M rows (TOKROWS loaded per sub-tile) x WN
@@ -69,7 +74,7 @@ struct GemmShape {
   static constexpr int offB = offA + STAGES * kAStage;
   static constexpr int offW = offB + DSTAGES * kBBuf;
   static constexpr int offBar = offW + STAGES * kWStage;
-  static constexpr int kNumBars = 2 * STAGES + DSTAGES + 4 + 1;
+  static constexpr int kNumBars = 4 * STAGES + DSTAGES + 4 + 1;
   static constexpr int offMisc = offBar + kNumBars * 8;
   static constexpr int offTab = offMisc + 8 * 4;
   static constexpr int kTabBytes = (kMaxGemmExperts * 4 + 1) * 4;
@@ -110,9 +115,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem + S::offA;
   uint8_t* sB = smem + S::offB;
   uint32_t* sW = reinterpret_cast<uint32_t*>(smem + S::offW);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);
-  uint64_t* empty = full + STAGES;
-  uint64_t* dfull = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::offBar);  // token stage loaded
+  uint64_t* empty = full + STAGES;    // token stage released by the MMA
+  uint64_t* wfull = empty + STAGES;   // packed-weight stage loaded
+  uint64_t* wempty = wfull + STAGES;  // packed-weight stage read by its dequant group
+  uint64_t* dfull = wempty + STAGES;
   uint64_t* tfull = dfull + DSTAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* fin = tempty + 2;
@@ -132,6 +139,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], kDeqWarps / DGROUPS);
     }
     for (int i = 0; i < DSTAGES; ++i) mbar_init(&dfull[i], kDeqWarps / DGROUPS);
     for (int i = 0; i < 2; ++i) {
@@ -163,27 +172,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   };
 
   if (warp == kProdWarp) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ token producer
     if (lane == 0) {
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
         int e, mt, nt;
         decode(tile, e, mt, nt);
-        const ExpertEntry* ent = table + e;
         const int row0 = s_start[e] + mt * ROWS;
-        const int n0 = nt * BO;
-        // PLAIN / SILU: one box of WJ words; SwiGLU: WJ/2 gate + WJ/2 up words
-        const CUtensorMap* wmap0;
-        if (kGLU) wmap0 = WN == 256 ? &ent->qw16[0] : &ent->qw8[0];
-        else wmap0 = WN == 256 ? &ent->qw32[mat] : &ent->qw16[mat];
-        const CUtensorMap* wmap1 = WN == 256 ? &ent->qw16[1] : &ent->qw8[1];
-        // descriptors were written to global memory by a copy before the launch
-        tensormap_acquire(wmap0);
-        if (kGLU) tensormap_acquire(wmap1);
-        // only the token box and the packed weight box(es) travel by TMA; the
-        // small per-group scale / zero rows are read by the dequant warps
-        const uint32_t tx = uint32_t(S::kAStage + S::kWStage);
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -191,11 +187,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], tx);
+          mbar_arrive_expect_tx(&full[s], uint32_t(S::kAStage));
           tma_load_2d(sA + s * S::kAStage, &tmap_a, &full[s], kb * kBK, row0);
-          uint32_t* w = sW + s * (S::kWStage / 4);
-          tma_load_2d(w, wmap0, &full[s], n0 / 8, kb * kBK);
-          if (kGLU) tma_load_2d(w + S::kWStage / 8, wmap1, &full[s], n0 / 8, kb * kBK);
         }
       }
       if (ok) {
@@ -212,6 +205,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int first = it - STAGES < 0 ? 0 : it - STAGES;
         for (int i = first; i < it; ++i) wait_drain(&full[i % STAGES], (i / STAGES) & 1);
       }
+    }
+  } else if (warp == kWProdWarp) {
+    // ------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+        int e, mt, nt;
+        decode(tile, e, mt, nt);
+        const ExpertEntry* ent = table + e;
+        const int n0 = nt * BO;
+        // PLAIN / SILU: one box of WJ words; SwiGLU: WJ/2 gate + WJ/2 up words
+        const CUtensorMap* wmap0;
+        if (kGLU) wmap0 = WN == 256 ? &ent->qw16[0] : &ent->qw8[0];
+        else wmap0 = WN == 256 ? &ent->qw32[mat] : &ent->qw16[mat];
+        const CUtensorMap* wmap1 = WN == 256 ? &ent->qw16[1] : &ent->qw8[1];
+        // descriptors were written to global memory by a copy before the launch
+        tensormap_acquire(wmap0);
+        if (kGLU) tensormap_acquire(wmap1);
+        // only the packed weight box(es) travel by TMA; the small per-group
+        // scale / zero rows are read by the dequant warps
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!wait_any(&wempty[s], ph ^ 1, s_abort, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&wfull[s], uint32_t(S::kWStage));
+          uint32_t* w = sW + s * (S::kWStage / 4);
+          tma_load_2d(w, wmap0, &wfull[s], n0 / 8, kb * kBK);
+          if (kGLU) tma_load_2d(w + S::kWStage / 8, wmap1, &wfull[s], n0 / 8, kb * kBK);
+        }
+      }
+      // Weight stages are released by ordinary arrivals of the dequant warps,
+      // so nothing arrives here after the loop; the last copies (which the
+      // dequant warps may not wait for after an abort) must land before the
+      // CTA exits.
+      (void)ok;
+      const int first = it - STAGES < 0 ? 0 : it - STAGES;
+      for (int i = first; i < it; ++i) wait_drain(&wfull[i % STAGES], (i / STAGES) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
@@ -232,6 +266,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * S::ACC);
+        // stacked M sub-tiles: a tile of at most 128 token rows (small experts,
+        // segment tails) skips the second sub-tile's MMAs; those accumulator
+        // rows are never read (the epilogue clips to the tile's rows)
+        int m_used = MT;
+        if (MT == 2) {
+          int e, mt, nt;
+          decode(tile, e, mt, nt);
+          if (s_len[e] - mt * ROWS <= 128) m_used = 1;
+        }
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -254,6 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t bdesc = umma_smem_desc(baddr + kk * 2048, 8192, 1024, 2);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
+              if (m >= m_used) break;
               // M sub-tile m: token rows 128m.. (16 KB into the stage), TMEM columns WN*m..
               const uint64_t adesc = umma_smem_desc(aaddr + m * 16384 + kk * 32, 16, 1024, 2);
               umma_f16_ss(d_tmem + uint32_t(m * WN), adesc, bdesc, idesc,
@@ -354,7 +398,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t ph = (it / STAGES) & 1;
         const int q = it % DSTAGES;
         const int prev = it - DSTAGES;  // last k-step that used buffer q
-        if (!wait_any(&full[s], ph, s_abort, err) ||
+        if (!wait_any(&wfull[s], ph, s_abort, err) ||
             (prev >= 0 &&
              !wait_any(&empty[prev % STAGES], (prev / STAGES) & 1, s_abort, err))) {
           ok = false;
@@ -383,6 +427,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                       ((cx ^ (rk & 7)) << 4)) = o;
           }
         }
+        // every packed word of the stage has been read and used: release it
+        // to the weight producer before the operand buffer is published
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty[s]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dfull[q]);

@@ -103,7 +103,8 @@ def _grouped_case(E, d, f, g, lens, mode, seed):
 @pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("lens,maxr", [([0, 1, 100, 300], 300), ([16, 16, 3, 0], 16),
                                        ([20, 7, 31, 12], 32), ([600, 260, 5, 129], 600),
-                                       ([64, 0, 33, 50], 64), ([128, 77, 1, 100], 128)])
+                                       ([64, 0, 33, 50], 64), ([128, 77, 1, 100], 128),
+                                       ([128, 256, 385, 0], 385)])
 def test_grouped_modes(mode, lens, maxr):
     from lightning_router.kernels.quantized_matmul import grouped_w4a16
     E, d, f, g = 4, 256, 384, 64
