@@ -204,8 +204,8 @@ int lr_encode_weight_table(const lr_expert_weights* experts, int E, int d_model,
 
 size_t lr_grouped_gemm_workspace_bytes(int num_experts);
 
-/* Grouped W4A16 GEMM on tcgen05 (swap-AB: weights are the 128-row UMMA M
- * operand, tokens the N operand).  For each expert e, rows
+/* Grouped W4A16 GEMM on tcgen05 (tokens are the UMMA M operand, dequantized
+ * weight columns the N operand).  For each expert e, rows
  * [seg_start[e], seg_start[e] + seg_len[e]) of A (R x K fp16, row-major)
  * are multiplied with matrix `mat` (or gate/up for SWIGLU) of expert e and
  * written to the same rows of C (R x N_out fp16).  seg_* live on the device.

@@ -53,6 +53,7 @@ def _plan_reference(counts: np.ndarray, rank: int, C: int) -> np.ndarray:
     ("prefill", dict(tokens=2048, d_model=1024, d_ff=2048)),
     ("fine", dict(tokens=1024, d_model=512)),
     ("decode", dict(tokens=64, d_model=1024, d_ff=2048)),
+    ("decode", dict(tokens=64, d_model=4096, d_ff=1024)),
 ])
 def test_peer_exchange_emulated_matches_single_gpu(world, wname, overrides):
     from lightning_router import _ext

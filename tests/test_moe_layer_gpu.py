@@ -73,6 +73,7 @@ def test_pr1_layer_matches_oracle():
 
 @pytest.mark.parametrize("name,overrides", [
     ("decode", dict(d_model=1024, d_ff=2048)),
+    ("decode", dict(d_model=4096, d_ff=7168)),
     ("fine", dict(tokens=1024, d_model=512)),
     ("prefill", dict(tokens=2048, d_model=512, d_ff=1024)),
     ("pr1", dict(tokens=333, capacity_factor=0.5)),
