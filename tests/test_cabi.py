@@ -45,6 +45,12 @@ def test_workspace_queries_are_host_only():
     assert lib.lr_gather_workspace_bytes(1000, 500) >= 4 * (1000 * 2 + 500 * 3)
     assert lib.lr_weight_table_bytes(8) == 8 * lib.lr_weight_table_bytes(1)
     assert lib.lr_weight_table_bytes(1) % 128 == 0
+    # gate + dispatch: covers both the one-launch path (T <= 256: ticket, 8 chunk
+    # partials of T x E fp32, T x k rows) and the two-kernel path
+    small = lib.lr_gate_dispatch_workspace_bytes(64, 2, 8)
+    assert small >= 256 + 8 * 64 * 8 * 4 + 64 * 2 * 4
+    assert small >= lib.lr_route_workspace_bytes(64, 2, 8)
+    assert lib.lr_gate_dispatch_workspace_bytes(4096, 2, 8) == lib.lr_route_workspace_bytes(4096, 2, 8)
 
 
 def test_argument_validation_without_device():
@@ -56,6 +62,12 @@ def test_argument_validation_without_device():
     assert lib.lr_topk_gating_dispatch(None, None, 4, 64, 65, 2, 8, ctypes.c_float(0.01), 0,
                                        None, None, None, None, None, None, None, None, None,
                                        None, None, ctypes.c_size_t(0), None, None) == -1
+    # gate + dispatch: d not a multiple of 16, E > 64, k > E, T = 0
+    nulls = [None] * 10  # the ten outputs after the logits
+    for T, d, E, k in [(4, 24, 8, 2), (4, 64, 65, 2), (4, 64, 4, 5), (0, 64, 8, 2)]:
+        assert lib.lr_gate_topk_gating_dispatch(
+            None, None, None, T, d, E, k, 8, ctypes.c_float(0.01), 0, None, *nulls,
+            None, ctypes.c_size_t(0), None, None) == -1
     # K not a multiple of 64
     assert lib.lr_grouped_w4a16_gemm(ctypes.c_void_p(128), 1, 0, 2, None, 4, 100, 64, None, None,
                                      4, None, None, ctypes.c_size_t(0), None, None) in (-1, -2)
@@ -63,8 +75,9 @@ def test_argument_validation_without_device():
 
 def test_torch_ops_register():
     ops = _ext.ops()
-    for name in ("gate_logits", "topk_gating_dispatch", "expert_routing_forward", "combine",
-                 "expert_routing_gather", "encode_weight_table", "grouped_w4a16_gemm"):
+    for name in ("gate_logits", "topk_gating_dispatch", "gate_topk_gating_dispatch",
+                 "expert_routing_forward", "combine", "expert_routing_gather",
+                 "encode_weight_table", "grouped_w4a16_gemm"):
         assert hasattr(ops, name), name
 
 
