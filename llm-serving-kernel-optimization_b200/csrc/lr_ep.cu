@@ -5,7 +5,7 @@
 // instead) done without a host round trip:
 //   * every rank keeps its tokens, the row -> token map of its uncapped expert
 //     segments and its expert outputs in buffers the other ranks have mapped
-//     (CUDA IPC, plain peer loads over NVLink; no multicast objects);
+//     (CUDA IPC, plain peer loads over NVLink; no NVLS or multimem objects);
 //   * lr_ep_plan turns the all-gathered per-(rank, expert) counts into the
 //     global slot-order capacity decision and both sides' row layouts, on the
 //     device;
