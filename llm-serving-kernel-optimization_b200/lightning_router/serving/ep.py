@@ -204,6 +204,14 @@ class ExpertParallelMoE:
     routing (aux is the global load-balancing loss).  ``exchange`` selects the
     token exchange ("peer" or "nccl", see the module notes); ``microbatches``
     applies to the NCCL exchange.
+
+    With the peer exchange, a forward whose shard size differs from this
+    rank's previous one re-agrees the sizes with a collective, so all ranks
+    must change their shard sizes in the same forward (the usual serving step:
+    a batch split evenly, or the same split, across the ranks).  A rank that
+    changes alone leaves that collective unmatched until the process group's
+    timeout.  Shards that vary independently per rank belong to
+    ``exchange="nccl"``, which gathers every rank's size in every forward.
     """
 
     def __init__(self, layer, world: int, rank: int, group=None, microbatches: int = 1,
