@@ -30,7 +30,7 @@ namespace lr {
 constexpr int kEpMaxCounts = 4096;  // G * E entries handled by the plan kernel
 
 struct EpPlanLayout {
-  int El, seg_start, seg_len, row_base, src_off, kept, my_off, my_kept, dst_row, total;
+  int El, seg_start, seg_len, row_base, src_off, kept, my_off, my_kept, dst_row, cap, total;
   __host__ __device__ EpPlanLayout(int G, int E) {
     El = E / G;
     seg_start = 0;
@@ -41,19 +41,25 @@ struct EpPlanLayout {
     my_off = kept + El * G;
     my_kept = my_off + E;
     dst_row = my_kept + E;
-    total = dst_row + E;
+    cap = dst_row + E;  // the capacity the plan applied
+    total = cap + 1;
   }
 };
 
 // One block.  counts[r*E + e] = slots of expert e on rank r (uncapped, in the
 // rank's slot order).  Rank r's slots of e follow those of lower ranks in the
 // global slot order, so kept(r, e) = clamp(C - sum_{r' < r} counts[r'][e], 0,
-// counts[r][e]) -- the single-GPU capacity rule.
+// counts[r][e]) -- the single-GPU capacity rule.  With shard_tokens (the G
+// ranks' token counts) C is max(int((k * sum T_r / E) * cf), 1) in double
+// precision, as on one GPU (reference kernels/expert_routing.py:196-197), and
+// capacity is the largest C the caller's buffers hold; otherwise C = capacity.
 __global__ void __launch_bounds__(256)
-    ep_plan_kernel(const int32_t* __restrict__ counts, int G, int E, int rank, int C,
+    ep_plan_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ shard_tokens,
+                   int G, int E, int top_k, double cf, int rank, int capacity,
                    int32_t* __restrict__ plan, int32_t* err) {
   __shared__ int s_cnt[kEpMaxCounts];
   __shared__ int s_kept[kEpMaxCounts];
+  __shared__ int s_cap;
   const EpPlanLayout L(G, E);
   for (int i = threadIdx.x; i < G * E; i += blockDim.x) {
     int c = counts[i];
@@ -63,7 +69,25 @@ __global__ void __launch_bounds__(256)
     }
     s_cnt[i] = c;
   }
+  if (threadIdx.x == 0) {
+    int C = capacity;
+    if (shard_tokens) {
+      long long T = 0;
+      for (int r = 0; r < G; ++r) {
+        const int t = shard_tokens[r];
+        if (t < 0) report(err, LR_DEVERR_BAD_SEGMENT);
+        else T += t;
+      }
+      const double q = double(T * top_k) / double(E);
+      const long long c = (long long)(q * cf);
+      C = c < 1 ? 1 : (c > capacity ? capacity : int(c));
+      if (c > capacity) report(err, LR_DEVERR_BAD_SEGMENT);  // buffers too small: rows clipped
+    }
+    s_cap = C;
+    plan[L.cap] = C;
+  }
   __syncthreads();
+  const int C = s_cap;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int base = 0;
     for (int r = 0; r < G; ++r) {
@@ -265,7 +289,22 @@ extern "C" int lr_ep_plan(const int32_t* counts, int world, int num_experts, int
   if (!counts || !plan || world < 1 || num_experts < 1 || num_experts % world ||
       rank < 0 || rank >= world || capacity < 1 || world * num_experts > kEpMaxCounts)
     return LR_ERR_INVALID_ARGUMENT;
-  ep_plan_kernel<<<1, 256, 0, stream>>>(counts, world, num_experts, rank, capacity, plan, err);
+  ep_plan_kernel<<<1, 256, 0, stream>>>(counts, nullptr, world, num_experts, 1, 1.0, rank,
+                                        capacity, plan, err);
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
+extern "C" int lr_ep_plan_tokens(const int32_t* counts, const int32_t* shard_tokens, int world,
+                                 int num_experts, int top_k, double capacity_factor, int rank,
+                                 int max_capacity, int32_t* plan, int32_t* err,
+                                 lr_stream_t stream) {
+  if (!counts || !shard_tokens || !plan || world < 1 || num_experts < 1 ||
+      num_experts % world || rank < 0 || rank >= world || top_k < 1 || !(capacity_factor > 0) ||
+      max_capacity < 1 || world * num_experts > kEpMaxCounts)
+    return LR_ERR_INVALID_ARGUMENT;
+  ep_plan_kernel<<<1, 256, 0, stream>>>(counts, shard_tokens, world, num_experts, top_k,
+                                        capacity_factor, rank, max_capacity, plan, err);
   LR_LAUNCH_CHECK();
   return LR_OK;
 }

@@ -29,11 +29,14 @@ Two exchanges implement the moves:
 * ``exchange="peer"`` (default with one process per GPU on one node): every rank
   keeps its tokens, the row -> token map of its expert segments and its expert
   outputs in buffers the other ranks map through CUDA IPC.  The plan is made on
-  the device from the all-gathered counts (``lr_ep_plan``), the expert owner
-  pulls its kept rows over NVLink (``lr_ep_gather``) and the token owner pulls
-  the output rows back while it combines them (``lr_ep_combine``).  No host
-  synchronisation; the counts all-gather and one 4-byte all-reduce after the
-  expert GEMMs order the peer reads.  Token shards must have equal sizes.
+  the device from the all-gathered shard sizes and counts (``lr_ep_plan_tokens``:
+  the capacity too), the expert owner pulls its kept rows over NVLink
+  (``lr_ep_gather``) and the token owner pulls the output rows back while it
+  combines them (``lr_ep_combine``).  No host synchronisation; the counts
+  all-gather and one 4-byte all-reduce after the expert GEMMs order the peer
+  reads.  The buffers are sized once for a per-rank shard limit, so shard sizes
+  may differ between ranks and change from step to step (each rank up to the
+  limit) while every rank issues the same collectives in every forward.
 * ``exchange="nccl"``: kept rows are permuted into a compact send buffer grouped
   by owner rank, exchanged with ``all_to_all_single`` and sent back the same
   way.  The split sizes need one device->host read of the gathered counts per
@@ -131,6 +134,15 @@ def plan_exchanges(stats: np.ndarray, rank: int, world: int, num_experts: int, t
     return plans
 
 
+def microbatch_bounds(num_tokens: int, nchunks: int) -> list:
+    """Token bounds of a shard's ``nchunks`` contiguous micro-batches.
+
+    ``nchunks`` is the same on every rank whatever its shard size (the gathered
+    statistics hold ``world * nchunks`` rows), so a small shard may have empty
+    micro-batches."""
+    return [num_tokens * c // nchunks for c in range(nchunks + 1)]
+
+
 def plan_exchange(stats: np.ndarray, rank: int, world: int, num_experts: int, top_k: int,
                   capacity_factor: float, load_balance_weight: float, chunk: int = 0,
                   nchunks: int = 1) -> ExchangePlan:
@@ -205,17 +217,18 @@ class ExpertParallelMoE:
     token exchange ("peer" or "nccl", see the module notes); ``microbatches``
     applies to the NCCL exchange.
 
-    With the peer exchange, a forward whose shard size differs from this
-    rank's previous one re-agrees the sizes with a collective, so all ranks
-    must change their shard sizes in the same forward (the usual serving step:
-    a batch split evenly, or the same split, across the ranks).  A rank that
-    changes alone leaves that collective unmatched until the process group's
-    timeout.  Shards that vary independently per rank belong to
-    ``exchange="nccl"``, which gathers every rank's size in every forward.
+    Shard sizes may differ between ranks and from one forward to the next.
+    The peer exchange sizes its mapped buffers once, for ``max_tokens_per_rank``
+    tokens per rank (when None: the largest shard of the first forward, agreed
+    by a collective that every rank enters in its first forward).  A shard above
+    that limit raises ``ValueError`` on its rank before any collective of the
+    step; the other ranks then fail at the process group's timeout, as after any
+    rank's error.  Every rank issues the same collectives in the same order in
+    every forward, whatever the sizes (an empty shard included).
     """
 
     def __init__(self, layer, world: int, rank: int, group=None, microbatches: int = 1,
-                 exchange: str = "peer"):
+                 exchange: str = "peer", max_tokens_per_rank: int | None = None):
         if layer.num_experts % world:
             raise ValueError("num_experts must be divisible by the world size")
         if exchange not in ("peer", "nccl"):
@@ -233,9 +246,10 @@ class ExpertParallelMoE:
         self.microbatches = max(1, int(microbatches))
         self.stage_events: list | None = None
         self._last_recv = 0
+        self._last_kept_e: list = []
         self._pinned: torch.Tensor | None = None  # reused host staging for per-step metadata
+        self.max_tokens_per_rank = max_tokens_per_rank
         self._peer: _PeerBuffers | None = None
-        self._peer_key = None
         self._plan: torch.Tensor | None = None
 
     def _to_device(self, arr: np.ndarray, dev, dtype) -> torch.Tensor:
@@ -256,15 +270,15 @@ class ExpertParallelMoE:
 
     @classmethod
     def from_layer(cls, layer, world: int, rank: int, group=None, microbatches: int = 1,
-                   exchange: str = "peer") -> "ExpertParallelMoE":
-        return cls(layer, world, rank, group, microbatches, exchange)
+                   exchange: str = "peer",
+                   max_tokens_per_rank: int | None = None) -> "ExpertParallelMoE":
+        return cls(layer, world, rank, group, microbatches, exchange, max_tokens_per_rank)
 
     def close(self) -> None:
         """Unmap the peers' exchange buffers (call before destroying the group)."""
         if self._peer is not None:
             self._peer.close()
             self._peer = None
-            self._peer_key = None
 
     def _mark(self, name):
         if self.stage_events is not None:
@@ -273,35 +287,38 @@ class ExpertParallelMoE:
             self.stage_events.append((name, ev))
 
     def last_kept_rows(self) -> int:
-        if self.exchange == "peer" and self._plan is not None:
-            return int(self._plan[self.El:2 * self.El].sum())
-        return self._last_recv
+        return int(sum(self.last_kept_per_expert()))
 
-    def _peer_buffers(self, T_l: int, d: int, dev) -> _PeerBuffers | None:
-        """Exchange buffers for this shard size (a collective when the size changes:
-        all ranks call forward with their new shards together).  None when the
-        shards differ in size (the NCCL exchange handles that)."""
-        key = (T_l, d, dev.index)
-        if self._peer_key != key:
-            sizes = [None] * self.world
-            dist.all_gather_object(sizes, T_l, group=self.group)
-            self.close()
-            self._peer_key = key
-            if any(t != T_l for t in sizes):
-                return None
-            C = expert_capacity(T_l * self.world * self.k, self.E, self.cf)
-            self._peer = _PeerBuffers(self.group, self.world, self.rank, dev, T_l, self.k, d,
-                                      self.El * C)
-            self._peer_C = C
+    def last_kept_per_expert(self) -> list:
+        """Kept rows of each local expert in the last forward."""
+        if self.exchange == "peer" and self._plan is not None:
+            return self._plan[self.El:2 * self.El].cpu().tolist()
+        return list(self._last_kept_e)
+
+    def _peer_buffers(self, T_l: int, d: int, dev) -> _PeerBuffers:
+        """The mapped exchange buffers, created in the first forward (a collective
+        every rank enters then) for the per-rank shard limit."""
+        if self._peer is None:
+            T_max = self.max_tokens_per_rank
+            if T_max is None:
+                sizes = [None] * self.world
+                dist.all_gather_object(sizes, int(T_l), group=self.group)
+                T_max = max(sizes)
+            T_max = max(int(T_max), 1)
+            C_max = expert_capacity(T_max * self.world * self.k, self.E, self.cf)
+            self._peer = _PeerBuffers(self.group, self.world, self.rank, dev, T_max, self.k, d,
+                                      self.El * C_max)
+            self._peer_C = C_max
+        if T_l > self._peer.T_max:
+            raise ValueError(f"shard of {T_l} tokens exceeds the expert-parallel limit of "
+                             f"{self._peer.T_max} tokens per rank (max_tokens_per_rank)")
         return self._peer
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor):
         if self.exchange == "peer" and self.world > 1:
             xf = x.reshape(-1, x.shape[-1])
-            bufs = self._peer_buffers(xf.shape[0], xf.shape[1], xf.device)
-            if bufs is not None:
-                return self._forward_peer(xf, bufs)
+            return self._forward_peer(xf, self._peer_buffers(xf.shape[0], xf.shape[1], xf.device))
         return self._forward_nccl(x)
 
     def _forward_peer(self, x: torch.Tensor, bufs: _PeerBuffers):
@@ -310,38 +327,49 @@ class ExpertParallelMoE:
         x = x.to(torch.float16).contiguous()
         T_l, d = x.shape
         E, G, El, k = self.E, self.world, self.El, self.k
-        C = self._peer_C
+        C_max = self._peer_C
         err = _ext.error_word(dev.index)
         self._mark("begin")
-        logits = self.layer.gate.logits(x)
-        self._mark("gate")
-        ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = ops.topk_route(logits, k, 1,
-                                                                         float(self.lbw), err)
-        # this rank's tokens and its uncapped row -> token map, readable by the owners
-        bufs.x[:T_l].copy_(x)
-        ops.route_rows(ids, gw, offs, pos, ws, T_l, E, bufs.src)
+        if T_l:
+            logits = self.layer.gate.logits(x)
+            self._mark("gate")
+            ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = ops.topk_route(
+                logits, k, 1, float(self.lbw), err)
+            # this rank's tokens and its uncapped row -> token map, readable by the owners
+            bufs.x[:T_l].copy_(x)
+            ops.route_rows(ids, gw, offs, pos, ws, T_l, E, bufs.src)
+            cnt = (offs[1:] - offs[:-1]).double()
+        else:  # an empty shard still takes part in every collective and owns its experts
+            self._mark("gate")
+            cnt = torch.zeros(E, dtype=torch.float64, device=dev)
+            psum = torch.zeros(E, dtype=torch.float64, device=dev)
         stats_l = torch.cat([torch.full((1,), float(T_l), dtype=torch.float64, device=dev),
-                             (offs[1:] - offs[:-1]).double(), psum])
+                             cnt, psum])
         stats = torch.empty(G * stats_l.numel(), dtype=torch.float64, device=dev)
         # after the writes above on every rank: the gather below may read them
         dist.all_gather_into_tensor(stats, stats_l, group=self.group)
         st = stats.view(G, -1)
         counts = st[:, 1:1 + E].round().to(torch.int32).contiguous()
-        plan = ops.ep_plan(counts, self.rank, C, err)
+        shard_tokens = st[:, 0].round().to(torch.int32).contiguous()
+        # capacity from the global slot count, decided on the device
+        plan = ops.ep_plan_tokens(counts, shard_tokens, self.rank, k, float(self.cf), C_max, err)
         a = ops.ep_gather(bufs.px, bufs.psrc, plan, E, self.rank, bufs.T_max, bufs.T_max * k,
                           d, bufs.a, err)
         self._mark("dispatch")
-        self.layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C,
+        self.layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C_max,
                                             first_expert=self.rank * El, num_local=El,
                                             mark=self._mark, out=bufs.y)
         # every owner's outputs are written before any rank reads them
         dist.all_reduce(bufs.flag, group=self.group)
         self._mark("a2a_combine")
-        out = ops.ep_combine(bufs.py, plan, ids, gw, pos, T_l, E, bufs.rows_max, d, err)
+        if T_l:
+            out = ops.ep_combine(bufs.py, plan, ids, gw, pos, T_l, E, bufs.rows_max, d, err)
+        else:
+            out = torch.empty(0, d, dtype=torch.float16, device=dev)
         self._mark("combine")
-        S = T_l * G * k
-        f = counts.sum(0).double() / float(max(S, 1))
-        P = st[:, 1 + E:].sum(0) / float(max(T_l * G, 1))
+        T_all = st[:, 0].sum()
+        f = counts.sum(0).double() / torch.clamp(T_all * k, min=1.0)
+        P = st[:, 1 + E:].sum(0) / torch.clamp(T_all, min=1.0)
         aux = (self.lbw * E * (f * P).sum()).float()
         self._plan = plan
         return out, aux
@@ -353,16 +381,22 @@ class ExpertParallelMoE:
         x = x.reshape(-1, x.shape[-1]).to(torch.float16).contiguous()
         T_l, d = x.shape
         E, G, El = self.E, self.world, self.El
-        nc = self.microbatches if T_l >= 256 * self.microbatches else 1
-        bounds = [T_l * c // nc for c in range(nc + 1)]
+        # the same micro-batch count on every rank (the gathered statistics have
+        # G * nc rows); a micro-batch of a small shard may be empty
+        nc = self.microbatches
+        bounds = microbatch_bounds(T_l, nc)
         err = _ext.error_word(dev.index)
         self._mark("begin")
-        logits = self.layer.gate.logits(x)
+        logits = self.layer.gate.logits(x) if T_l else None
         self._mark("gate")
         # phase 1 for every micro-batch, then one gather of all shard statistics
         routes, stats_l = [], []
         for c in range(nc):
             lo, hi = bounds[c], bounds[c + 1]
+            if hi == lo:
+                routes.append(None)
+                stats_l.append(torch.zeros(1 + 2 * E, dtype=torch.float64, device=dev))
+                continue
             r = ops.topk_route(logits[lo:hi], self.k, 1, float(self.lbw), err)
             ids, gw, _tok, offs, _kept, _aux, psum, pos, ws = r
             routes.append((ids, gw, pos, ws))
@@ -377,17 +411,20 @@ class ExpertParallelMoE:
         # phase 2 + dispatch exchange for every micro-batch (asynchronous collectives)
         sends, recvs, metas, dwork = [], [], [], []
         for c, plan in enumerate(plans):
-            ids, gw, pos, ws = routes[c]
             idx_h = plan.reorder if (plan.reorder is not None and plan.n_recv) else \
                 np.zeros(0, np.int64)
             meta = self._to_device(np.concatenate([plan.rank_base, plan.koff, plan.seg_start,
                                                    plan.seg_len, idx_h]).astype(np.int32),
                                    dev, torch.int32)
             metas.append(meta)
-            xs = x[bounds[c]:bounds[c + 1]]
-            send, _rw, _src = ops.permute_tokens(xs, ids, gw, meta[E:2 * E + 1], meta[:E],
-                                                 plan.capacity, True, False, pos, ws,
-                                                 plan.n_send, E)
+            if routes[c] is not None:
+                ids, gw, pos, ws = routes[c]
+                xs = x[bounds[c]:bounds[c + 1]]
+                send, _rw, _src = ops.permute_tokens(xs, ids, gw, meta[E:2 * E + 1], meta[:E],
+                                                     plan.capacity, True, False, pos, ws,
+                                                     plan.n_send, E)
+            else:  # an empty micro-batch sends nothing
+                send = torch.empty(1, d, dtype=torch.float16, device=dev)
             recv = torch.empty(max(plan.n_recv, 1), d, dtype=torch.float16, device=dev)
             sends.append(send)
             recvs.append(recv)
@@ -428,9 +465,13 @@ class ExpertParallelMoE:
             cwork[c].wait()
             if c == 0:
                 self._mark("a2a_combine")
+            if routes[c] is None:
+                outs.append(torch.empty(0, d, dtype=torch.float16, device=dev))
+                continue
             _ids, gw, pos, _ws = routes[c]
             outs.append(combine(backs[c], gw, pos, bounds[c + 1] - bounds[c], self.k))
         out = outs[0] if nc == 1 else torch.cat(outs)
         self._mark("combine")
         self._last_recv = sum(p.n_recv for p in plans)
+        self._last_kept_e = [int(sum(int(p.seg_len[el]) for p in plans)) for el in range(El)]
         return out, torch.tensor(plans[0].aux_loss, dtype=torch.float32, device=dev)

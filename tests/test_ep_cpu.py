@@ -206,3 +206,125 @@ def test_microbatch_plans_follow_global_slot_order(world, nchunks, E, k, cf):
                 assert sorted(p.reorder.tolist()) == list(range(p.n_recv))
             assert int(p.seg_len.sum()) == p.n_recv
     np.testing.assert_array_equal(np.concatenate(got), r_ref.kept)
+
+
+def _rank_main_chunks(rank, world, port, cfg, q):
+    """One rank of the NCCL exchange's host logic with unequal shards and
+    micro-batches: every rank splits its shard with ``microbatch_bounds`` into the
+    same number of micro-batches (some may be empty), gathers one statistics row
+    per micro-batch, and exchanges each micro-batch's kept rows."""
+    try:
+        from lightning_router.serving.ep import microbatch_bounds, plan_exchanges
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=30))
+        shards, nc, d, f, E, k, cf, seed = cfg
+        T = sum(shards)
+        x, logits, experts = _problem(T, d, f, E, k, seed)
+        lo0 = sum(shards[:rank])
+        xs, ls = x[lo0:lo0 + shards[rank]], logits[lo0:lo0 + shards[rank]]
+        bounds = microbatch_bounds(shards[rank], nc)
+        routes, stats_l = [], []
+        for c in range(nc):
+            lo, hi = bounds[c], bounds[c + 1]
+            if hi == lo:
+                routes.append(None)
+                stats_l.append(np.zeros(1 + 2 * E))
+                continue
+            ids, w, probs = orc.topk_gating(ls[lo:hi], k)
+            ids, w = ids.reshape(-1), w.reshape(-1)
+            routes.append((ids, w))
+            stats_l.append(np.concatenate([[hi - lo], np.bincount(ids, minlength=E),
+                                           probs.astype(np.float64).sum(0)]))
+        stats_l = torch.from_numpy(np.concatenate(stats_l).astype(np.float64))
+        stats = torch.zeros(world * stats_l.numel(), dtype=torch.float64)
+        dist.all_gather_into_tensor(stats, stats_l)  # equal sizes on every rank
+        plans = plan_exchanges(stats.view(world * nc, -1).numpy(), rank, world, E, k, cf, 0.01,
+                               nc)
+        out = np.zeros((shards[rank], d), np.float32)
+        kept_l = []
+        El = E // world
+        for c, plan in enumerate(plans):
+            lo, hi = bounds[c], bounds[c + 1]
+            send = np.zeros((plan.n_send, d), np.float16)
+            if routes[c] is not None:
+                ids, w = routes[c]
+                counts = np.bincount(ids, minlength=E)
+                order = np.argsort(ids, kind="stable")
+                local_rank = np.empty_like(ids)
+                local_rank[order] = np.arange(ids.size) - (np.cumsum(counts) - counts)[ids[order]]
+                kept = plan.rank_base[ids] + local_rank < plan.capacity
+                pos = np.full(ids.size, -1, np.int64)
+                tok = np.repeat(np.arange(hi - lo), k)
+                for s_ in np.nonzero(kept)[0]:
+                    pos[s_] = plan.koff[ids[s_]] + local_rank[s_]
+                    send[pos[s_]] = xs[lo + tok[s_]]
+                kept_l.append(kept)
+            recv = torch.zeros(plan.n_recv, d, dtype=torch.float16)
+            dist.all_to_all_single(recv, torch.from_numpy(send), plan.recv_rows, plan.send_rows)
+            rr = recv.numpy()
+            a = rr[plan.reorder] if plan.reorder is not None else rr
+            y = np.zeros((plan.n_recv, d), np.float32)
+            for el in range(El):
+                st, n = int(plan.seg_start[el]), int(plan.seg_len[el])
+                if n:
+                    ex = experts[rank * El + el]
+                    y[st:st + n] = orc.expert_ffn(a[st:st + n], ex["up"], ex["down"], ex["gate"])
+            y_send = np.empty_like(y)
+            if plan.reorder is not None:
+                y_send[plan.reorder] = y
+            else:
+                y_send = y
+            back = torch.zeros(plan.n_send, d, dtype=torch.float32)
+            dist.all_to_all_single(back, torch.from_numpy(y_send), plan.send_rows,
+                                   plan.recv_rows)
+            if routes[c] is not None:
+                bk = back.numpy()
+                for s_ in np.nonzero(kept)[0]:
+                    out[lo + tok[s_]] += w[s_] * bk[pos[s_]]
+        full = [None] * world
+        dist.all_gather_object(full, (out, np.concatenate(kept_l) if kept_l else
+                                      np.zeros(0, bool), plans[0].aux_loss))
+        if rank == 0:
+            q.put(("ok", np.concatenate([f_[0] for f_ in full]),
+                   np.concatenate([f_[1] for f_ in full]), full[0][2]))
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("err", traceback.format_exc(), None, None))
+
+
+@pytest.mark.parametrize("shards,nc,E,k,cf", [([70, 9], 2, 4, 2, 1.0), ([0, 96], 2, 8, 2, 1.25),
+                                              ([33, 1, 50, 2], 2, 8, 2, 0.9),
+                                              ([5, 40], 3, 4, 1, 1.5)])
+def test_unequal_shards_with_microbatches_match_oracle(shards, nc, E, k, cf):
+    """Unequal (and empty) shards with several micro-batches: the statistics rows
+    agree in number across ranks, and the result equals the single-process oracle."""
+    world = len(shards)
+    cfg = (shards, nc, 32, 48, E, k, cf, 4321 + sum(shards))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_chunks, args=(r, world, port, cfg, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "ok", res[1]
+    _, got, kept_got, aux_got = res
+    x, logits, experts = _problem(sum(shards), 32, 48, E, k, cfg[-1])
+    ref, aux, r = orc.moe_layer(x, logits, k, cf, experts)
+    np.testing.assert_array_equal(kept_got.astype(bool), r.kept)
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+    assert abs(aux_got - aux) <= 1e-9 + 1e-7 * abs(aux)
+
+
+def test_microbatch_bounds_are_rank_independent():
+    from lightning_router.serving.ep import microbatch_bounds
+    for T in (0, 1, 5, 255, 256, 4096):
+        for nc in (1, 2, 3):
+            b = microbatch_bounds(T, nc)
+            assert len(b) == nc + 1 and b[0] == 0 and b[-1] == T
+            assert all(b[i] <= b[i + 1] for i in range(nc))

@@ -45,7 +45,7 @@ def _plan_reference(counts: np.ndarray, rank: int, C: int) -> np.ndarray:
         o, el = divmod(e, El)
         dst_row[e] = kept[:, o * El:o * El + el].sum() + kept[:rank, e].sum()
     return np.concatenate([seg_start, seg_len, row_base.ravel(), src_off.ravel(), kp.ravel(),
-                           my_off, my_kept, dst_row]).astype(np.int32)
+                           my_off, my_kept, dst_row, [C]]).astype(np.int32)
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -97,4 +97,69 @@ def test_peer_exchange_emulated_matches_single_gpu(world, wname, overrides):
     _ext.check_device_errors()
     full = torch.cat(outs)
     ref, _ = layer(t.x)
+    assert torch.equal(full, ref), f"max |diff| {(full.float() - ref.float()).abs().max()}"
+
+
+@pytest.mark.parametrize("shards,wname,overrides", [
+    ([300, 212], "prefill", dict(d_model=1024, d_ff=2048)),
+    ([1, 40, 0, 37], "fine", dict(d_model=512)),
+    ([5, 27], "decode", dict(d_model=1024, d_ff=2048)),
+])
+def test_peer_exchange_unequal_shards_emulated(shards, wname, overrides):
+    """Ranks with different (and empty) shards: the capacity is decided on the device
+    from the gathered shard sizes (``lr_ep_plan_tokens``), buffers are sized for the
+    largest shard, and the result equals the single-GPU layer on the whole batch."""
+    from lightning_router import _ext
+    from lightning_router.kernels.expert_routing import expert_capacity
+    from lightning_router.workloads import WORKLOADS, build_layer
+    T = sum(shards)
+    w = dataclasses.replace(WORKLOADS[wname], tokens=T, **overrides)
+    dev = torch.device("cuda", 0)
+    layer, t = build_layer(w, device=dev)
+    ops = _ext.ops()
+    err = _ext.error_word(0)
+    _ext.check_device_errors()
+    E, k, G, d = w.experts, w.top_k, len(shards), w.d_model
+    El = E // G
+    T_max = max(shards)
+    C = expert_capacity(T * k, E, w.capacity_factor)
+    C_max = expert_capacity(T_max * G * k, E, w.capacity_factor)
+    rows_max = El * C_max
+    ranks, lo = [], 0
+    for r, Tl in enumerate(shards):
+        rk = dict(T=Tl, x=torch.zeros(T_max, d, dtype=torch.float16, device=dev),
+                  src=torch.zeros(T_max * k, dtype=torch.int32, device=dev),
+                  y=torch.empty(rows_max, d, dtype=torch.float16, device=dev),
+                  a=torch.empty(rows_max, d, dtype=torch.float16, device=dev),
+                  cnt=torch.zeros(E, dtype=torch.int32, device=dev))
+        if Tl:
+            x = t.x[lo:lo + Tl].contiguous()
+            logits = layer.gate.logits(x)
+            ids, gw, _tok, offs, _kept, _aux, _psum, pos, ws = ops.topk_route(
+                logits, k, 1, float(layer.gate.load_balance_weight), err)
+            rk["x"][:Tl].copy_(x)
+            ops.route_rows(ids, gw, offs, pos, ws, Tl, E, rk["src"])
+            rk.update(ids=ids, gw=gw, pos=pos, cnt=(offs[1:] - offs[:-1]).int())
+        ranks.append(rk)
+        lo += Tl
+    counts = torch.stack([rk["cnt"] for rk in ranks]).contiguous()
+    sizes = torch.tensor(shards, dtype=torch.int32, device=dev)
+    px = torch.tensor([rk["x"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    psrc = torch.tensor([rk["src"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    py = torch.tensor([rk["y"].data_ptr() for rk in ranks], dtype=torch.int64, device=dev)
+    cnt_h = counts.cpu().numpy().astype(np.int64)
+    for r, rk in enumerate(ranks):
+        plan = ops.ep_plan_tokens(counts, sizes, r, k, float(w.capacity_factor), C_max, err)
+        assert np.array_equal(plan.cpu().numpy(), _plan_reference(cnt_h, r, C))
+        a = ops.ep_gather(px, psrc, plan, E, r, T_max, T_max * k, d, rk["a"], err)
+        layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C_max,
+                                       first_expert=r * El, num_local=El, out=rk["y"])
+        rk["plan"] = plan
+    outs = [ops.ep_combine(py, rk["plan"], rk["ids"], rk["gw"], rk["pos"], rk["T"], E, rows_max,
+                           d, err) for rk in ranks if rk["T"]]
+    _ext.check_device_errors()
+    full = torch.cat(outs)
+    ref, _ = layer(t.x)
+    # the GEMM's tile class is chosen from the buffers' row bound (C_max); these
+    # cases keep it equal to the single-GPU one, so the rows match bit for bit
     assert torch.equal(full, ref), f"max |diff| {(full.float() - ref.float()).abs().max()}"
