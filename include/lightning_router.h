@@ -196,25 +196,31 @@ typedef struct lr_expert_weights {
 
 /* Host-side encoding of the per-expert weight table (TMA descriptors and
  * pointers).  Writes `lr_weight_table_bytes(E)` bytes into `host_table`
- * (64-byte aligned host memory); the caller copies it to a 64-byte aligned
- * device buffer once per weight set.  No CUDA calls besides descriptor encoding. */
+ * (128-byte aligned host memory); the caller copies it to a 128-byte aligned
+ * device buffer once per weight set.  No CUDA calls besides descriptor encoding.
+ * Accepts every shape of the packed format: K % group_size == 0, N % 8 == 0
+ * (reference lightning_router/quantization/pack_weights.py:44-45).          */
 size_t lr_weight_table_bytes(int num_experts);
 int lr_encode_weight_table(const lr_expert_weights* experts, int E, int d_model, int d_ff,
                            int group_size, int gated, void* host_table, size_t table_bytes);
 
 size_t lr_grouped_gemm_workspace_bytes(int num_experts);
 
-/* Grouped W4A16 GEMM on tcgen05 (tokens are the UMMA M operand, dequantized
- * weight columns the N operand).  For each expert e, rows
+/* Grouped W4A16 GEMM.  For each expert e, rows
  * [seg_start[e], seg_start[e] + seg_len[e]) of A (R x K fp16, row-major)
  * are multiplied with matrix `mat` (or gate/up for SWIGLU) of expert e and
  * written to the same rows of C (R x N_out fp16).  seg_* live on the device.
  * `max_rows_per_expert` bounds seg_len (selects the token tile); seg_len
- * beyond it is clamped and flagged.
+ * beyond it is clamped and flagged.  `group_size` is the one the table was
+ * encoded with.  The kernel follows the shape: tcgen05 (tokens the UMMA M
+ * operand) when K % 64 == 0, group_size % 64 == 0 and N % 32 == 0; mma.sync
+ * with the weights as the M operand when K % 8 == 0, N % 32 == 0 and
+ * group_size is a power of two >= 16; otherwise CUDA cores.  A needs 2-byte,
+ * C 16-byte alignment.
  * Replaces ExpertGroup.forward / ExpertFFN._qmatmul + quantized_matmul
  * (lightning_router/models/experts.py:58-121, kernels/quantized_matmul.py:122-173). */
 int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, int mat,
-                          const void* A, int R, int K, int N,
+                          const void* A, int R, int K, int N, int group_size,
                           const int32_t* seg_start, const int32_t* seg_len,
                           int max_rows_per_expert, void* C, void* workspace,
                           size_t workspace_bytes, int32_t* err, lr_stream_t stream);
@@ -224,8 +230,8 @@ int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, int mat,
  * `device_table` holds one expert entry encoded with gated = 0 whose matrix 2
  * is (qweight, scales, zeros) with K = d_ff, N = d_model.                     */
 int lr_quantized_matmul(const void* device_table, const void* A, int M, int K, int N,
-                        void* C, void* workspace, size_t workspace_bytes, int32_t* err,
-                        lr_stream_t stream);
+                        int group_size, void* C, void* workspace, size_t workspace_bytes,
+                        int32_t* err, lr_stream_t stream);
 
 /* ---- expert-parallel exchange over NVLink peer memory --------------------
  * Replaces the all-GPU expert execution + host all-reduce of the reference's
@@ -249,6 +255,17 @@ int lr_ep_plan_size(int world, int num_experts);
  * Limits: G * E <= 4096.                                                     */
 int lr_ep_plan(const int32_t* counts, int world, int num_experts, int rank, int capacity,
                int32_t* plan, int32_t* err, lr_stream_t stream);
+
+/* lr_ep_plan with the capacity computed on the device from the G ranks' token
+ * counts (shard_tokens, int32 [G]): C = max(int((top_k * sum T_r / E) *
+ * capacity_factor), 1) in double precision, the single-GPU formula (reference
+ * kernels/expert_routing.py:196-197), so shards may differ in size from rank
+ * to rank and from step to step with no host round trip.  max_capacity is
+ * the largest C the caller's buffers hold; a larger C is clipped to it and
+ * flagged in err.  The plan's last entry holds the C it applied.             */
+int lr_ep_plan_tokens(const int32_t* counts, const int32_t* shard_tokens, int world,
+                      int num_experts, int top_k, double capacity_factor, int rank,
+                      int max_capacity, int32_t* plan, int32_t* err, lr_stream_t stream);
 
 /* Expert owner: rows of its segments <- the kept token rows, read from the
  * source ranks' token buffers (tokens < max_tokens, map entries < max_slots).

@@ -30,13 +30,19 @@ int record_cuda_error(cudaError_t e);  // defined in lr_capi.cu
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device
 // (the attribute belongs to the kernel's copy in each device's context).
 // `done` is a per-kernel bit set over device ordinals.
+// With max_carveout the kernel also asks for the largest shared-memory share of
+// the SM's L1 (so that several CTAs with large rings fit on an SM).
 template <class Kernel>
-inline int set_dyn_smem_once(Kernel kern, int bytes, unsigned long long& done) {
+inline int set_dyn_smem_once(Kernel kern, int bytes, unsigned long long& done,
+                             bool max_carveout = false) {
   int dev = 0;
   LR_CUDA_TRY(cudaGetDevice(&dev));
   const unsigned long long bit = 1ull << (dev & 63);
   if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return 0;
   LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (max_carveout)
+    LR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     int(cudaSharedmemCarveoutMaxShared)));
   __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
   return 0;
 }

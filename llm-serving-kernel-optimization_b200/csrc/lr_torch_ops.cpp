@@ -345,7 +345,7 @@ at::Tensor encode_weight_table(const std::vector<c10::optional<at::Tensor>>& qwe
 }
 
 at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int64_t mode,
-                              int64_t mat, const at::Tensor& A, int64_t N,
+                              int64_t mat, const at::Tensor& A, int64_t N, int64_t group_size,
                               const c10::optional<at::Tensor>& seg_start,
                               const c10::optional<at::Tensor>& seg_len, int64_t max_rows,
                               const c10::optional<at::Tensor>& out,
@@ -373,8 +373,9 @@ at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int6
     sl = seg_len->data_ptr<int32_t>();
   }
   check_status(lr_grouped_w4a16_gemm(table.data_ptr(), int(num_experts), int(mode), int(mat),
-                                     A.data_ptr(), int(A.size(0)), int(A.size(1)), int(N), ss, sl,
-                                     int(max_rows), C.data_ptr(), nullptr, 0, err_ptr(err),
+                                     A.data_ptr(), int(A.size(0)), int(A.size(1)), int(N),
+                                     int(group_size), ss, sl, int(max_rows), C.data_ptr(), nullptr,
+                                     0, err_ptr(err),
                                      cur_stream()),
                "grouped_w4a16_gemm");
   return C;
@@ -417,6 +418,29 @@ at::Tensor ep_plan(const at::Tensor& counts, int64_t rank, int64_t capacity,
   check_status(lr_ep_plan(counts.data_ptr<int32_t>(), G, E, int(rank), int(capacity),
                           plan.data_ptr<int32_t>(), err_ptr(err), cur_stream()),
                "ep_plan");
+  return plan;
+}
+
+// Plan with the capacity from the all-gathered shard sizes (int32 [G]).
+at::Tensor ep_plan_tokens(const at::Tensor& counts, const at::Tensor& shard_tokens, int64_t rank,
+                          int64_t top_k, double capacity_factor, int64_t max_capacity,
+                          const c10::optional<at::Tensor>& err) {
+  check_cuda(counts, "counts");
+  check_cuda(shard_tokens, "shard_tokens");
+  TORCH_CHECK(counts.dim() == 2 && counts.scalar_type() == at::kInt && counts.is_contiguous(),
+              "counts: contiguous (G, E) int32");
+  TORCH_CHECK(shard_tokens.scalar_type() == at::kInt && shard_tokens.is_contiguous() &&
+                  shard_tokens.numel() == counts.size(0),
+              "shard_tokens: contiguous (G,) int32");
+  c10::cuda::CUDAGuard g(counts.device());
+  const int G = int(counts.size(0)), E = int(counts.size(1));
+  const int n = lr_ep_plan_size(G, E);
+  TORCH_CHECK(n > 0, "ep_plan_tokens: E must be a multiple of G");
+  auto plan = at::empty({n}, counts.options());
+  check_status(lr_ep_plan_tokens(counts.data_ptr<int32_t>(), shard_tokens.data_ptr<int32_t>(), G,
+                                 E, int(top_k), capacity_factor, int(rank), int(max_capacity),
+                                 plan.data_ptr<int32_t>(), err_ptr(err), cur_stream()),
+               "ep_plan_tokens");
   return plan;
 }
 
@@ -490,11 +514,15 @@ TORCH_LIBRARY(lightning_router, m) {
       "num_experts, int d_model, int d_ff, int group_size, bool gated) -> Tensor");
   m.def(
       "grouped_w4a16_gemm(Tensor table, int num_experts, int mode, int mat, Tensor A, int N, "
-      "Tensor? seg_start, Tensor? seg_len, int max_rows, Tensor? out, Tensor? err) -> Tensor");
+      "int group_size, Tensor? seg_start, Tensor? seg_len, int max_rows, Tensor? out, "
+      "Tensor? err) -> Tensor");
   m.def(
       "route_rows(Tensor expert_ids, Tensor gate_weights, Tensor row_offsets, Tensor(a!) "
       "slot_pos, Tensor ws, int num_tokens, int num_experts, Tensor(b!) source_idx) -> Tensor");
   m.def("ep_plan(Tensor counts, int rank, int capacity, Tensor? err) -> Tensor");
+  m.def(
+      "ep_plan_tokens(Tensor counts, Tensor shard_tokens, int rank, int top_k, float cf, "
+      "int max_capacity, Tensor? err) -> Tensor");
   m.def(
       "ep_gather(Tensor peer_tokens, Tensor peer_source_idx, Tensor plan, int num_experts, "
       "int rank, int max_tokens, int max_slots, int d, Tensor(a!) out, Tensor? err) -> Tensor");
@@ -516,6 +544,7 @@ TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
   m.impl("grouped_w4a16_gemm", &grouped_w4a16_gemm);
   m.impl("route_rows", &route_rows);
   m.impl("ep_plan", &ep_plan);
+  m.impl("ep_plan_tokens", &ep_plan_tokens);
   m.impl("ep_gather", &ep_gather);
   m.impl("ep_combine", &ep_combine);
 }

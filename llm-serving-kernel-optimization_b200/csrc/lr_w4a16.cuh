@@ -15,12 +15,14 @@ struct alignas(128) ExpertEntry {
   CUtensorMap qw32[3];  // packed weights, box {32 words = 256 features, 64 rows}
   CUtensorMap qw16[3];  // packed weights, box {16 words = 128 features, 64 rows}
   CUtensorMap qw8[3];   // packed weights, box {8 words = 64 features, 64 rows}
+  const int32_t* qw[3];
   const __half* scales[3];
   const int32_t* zeros[3];
   int32_t K[3];
   int32_t N[3];
   int32_t group_size;
   int32_t present;  // bit m set when matrix m is encoded
+  int32_t tma;      // bit m set when matrix m's tensor maps are encoded (N % 32 == 0)
 };
 static_assert(sizeof(ExpertEntry) % 128 == 0, "table entry alignment");
 
@@ -152,6 +154,22 @@ inline int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LR_OK : LR_ERR_INVALID_ARGUMENT;
 }
+
+// Grouped GEMM for expert segments of at most kSkinnyMaxRows rows (decode):
+// mma.sync with the weights as the M operand (lr_w4a16_skinny.cu).  Needs
+// K % 8 == 0 (16-byte token rows for TMA) and a group size that is a power of
+// two >= 16.
+constexpr int kSkinnyMaxRows = 32;
+// Grouped GEMM for any shape of the packed format (lr_w4a16_generic.cu): CUDA
+// cores, for what neither TMA-fed kernel takes.
+template <int MODE>
+int launch_generic(const void* A, int K, int R, const ExpertEntry* table, int E, int mat, int N,
+                   int group_size, const int32_t* seg_start, const int32_t* seg_len,
+                   int max_rows, __half* C, int32_t* err, cudaStream_t stream);
+template <int MODE>
+int launch_skinny(const void* A, int K, int R, const ExpertEntry* table, int E, int mat, int N,
+                  const int32_t* seg_start, const int32_t* seg_len, int max_rows, __half* C,
+                  int32_t* err, cudaStream_t stream);
 
 }  // namespace lr
 

@@ -580,7 +580,7 @@ extern "C" int lr_encode_weight_table(const lr_expert_weights* experts, int E, i
   if (!experts || E < 1 || E > kMaxGemmExperts || !host_table) return LR_ERR_INVALID_ARGUMENT;
   if (table_bytes < lr_weight_table_bytes(E)) return LR_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(host_table) & 127u) != 0) return LR_ERR_INVALID_ARGUMENT;
-  if (group_size < kBK || group_size % kBK != 0) return LR_ERR_UNSUPPORTED;
+  if (group_size < 1) return LR_ERR_INVALID_ARGUMENT;
   ExpertEntry* tab = static_cast<ExpertEntry*>(host_table);
   memset(tab, 0, sizeof(ExpertEntry) * size_t(E));
   for (int e = 0; e < E; ++e) {
@@ -592,19 +592,25 @@ extern "C" int lr_encode_weight_table(const lr_expert_weights* experts, int E, i
       const int N = (m < 2) ? d_ff : d_model;
       const int32_t* qw = experts[e].qweight[m];
       if (!qw) continue;
-      if (K % kBK != 0 || K % group_size != 0 || N % 32 != 0) return LR_ERR_UNSUPPORTED;
+      // the packed format's own limits (reference pack_weights.py:44-45)
+      if (K < 1 || K % group_size != 0 || N < 8 || N % 8 != 0) return LR_ERR_UNSUPPORTED;
       if (!experts[e].scales[m] || !experts[e].zeros[m]) return LR_ERR_INVALID_ARGUMENT;
       if ((reinterpret_cast<uintptr_t>(qw) | reinterpret_cast<uintptr_t>(experts[e].scales[m]) |
            reinterpret_cast<uintptr_t>(experts[e].zeros[m])) & 15u)
         return LR_ERR_INVALID_ARGUMENT;
-      CUtensorMap* maps[3] = {&ent.qw32[m], &ent.qw16[m], &ent.qw8[m]};
-      const uint32_t words[3] = {32, 16, 8};
-      for (int b = 0; b < 3; ++b) {
-        const int rc = encode_2d(maps[b], CU_TENSOR_MAP_DATA_TYPE_INT32, qw, uint64_t(N / 8),
-                                 uint64_t(K), uint64_t(N / 8) * 4, words[b], kBK,
-                                 CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (rc) return rc;
+      // TMA strides are multiples of 16 bytes: N / 8 words per packed row
+      if (N % 32 == 0) {
+        CUtensorMap* maps[3] = {&ent.qw32[m], &ent.qw16[m], &ent.qw8[m]};
+        const uint32_t words[3] = {32, 16, 8};
+        for (int b = 0; b < 3; ++b) {
+          const int rc = encode_2d(maps[b], CU_TENSOR_MAP_DATA_TYPE_INT32, qw, uint64_t(N / 8),
+                                   uint64_t(K), uint64_t(N / 8) * 4, words[b], kBK,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+          if (rc) return rc;
+        }
+        ent.tma |= 1 << m;
       }
+      ent.qw[m] = qw;
       ent.scales[m] = static_cast<const __half*>(experts[e].scales[m]);
       ent.zeros[m] = experts[e].zeros[m];
       ent.K[m] = K;
@@ -621,43 +627,53 @@ extern "C" size_t lr_grouped_gemm_workspace_bytes(int num_experts) {
 }
 
 extern "C" int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, int mat,
-                                     const void* A, int R, int K, int N, const int32_t* seg_start,
-                                     const int32_t* seg_len, int max_rows_per_expert, void* C,
-                                     void* workspace, size_t workspace_bytes, int32_t* err,
-                                     lr_stream_t stream) {
+                                     const void* A, int R, int K, int N, int group_size,
+                                     const int32_t* seg_start, const int32_t* seg_len,
+                                     int max_rows_per_expert, void* C, void* workspace,
+                                     size_t workspace_bytes, int32_t* err, lr_stream_t stream) {
   (void)workspace;
   (void)workspace_bytes;
   if (!device_table || E < 1 || E > kMaxGemmExperts) return LR_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(device_table) & 127u) != 0) return LR_ERR_INVALID_ARGUMENT;
   if (mode < LR_FFN_MODE_PLAIN || mode > LR_FFN_MODE_SWIGLU) return LR_ERR_INVALID_ARGUMENT;
   if (mode != LR_FFN_MODE_SWIGLU && (mat < 0 || mat > 2)) return LR_ERR_INVALID_ARGUMENT;
-  if (K < kBK || K % kBK != 0) return LR_ERR_UNSUPPORTED;
-  if (N < 32 || N % 32 != 0) return LR_ERR_UNSUPPORTED;
+  if (K < 1 || group_size < 1 || K % group_size != 0) return LR_ERR_INVALID_ARGUMENT;
+  if (N < 8 || N % 8 != 0) return LR_ERR_UNSUPPORTED;
   if (R < 0 || max_rows_per_expert < 0) return LR_ERR_INVALID_ARGUMENT;
   if (R == 0 || max_rows_per_expert == 0) return LR_OK;
-  if (!A || !C || ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(C)) & 15u))
+  if (!A || !C || (reinterpret_cast<uintptr_t>(A) & 1u) || (reinterpret_cast<uintptr_t>(C) & 15u))
     return LR_ERR_INVALID_ARGUMENT;
   if ((seg_start == nullptr) != (seg_len == nullptr)) return LR_ERR_INVALID_ARGUMENT;
   if (!seg_start && E != 1) return LR_ERR_INVALID_ARGUMENT;
   const ExpertEntry* tab = static_cast<const ExpertEntry*>(device_table);
   __half* Cp = static_cast<__half*>(C);
   const int mr = max_rows_per_expert;
+  const int g = group_size;
+  // Kernel by shape: the tensor maps exist for N % 32 == 0; the token operand
+  // goes through TMA when its rows are 16-byte aligned (K % 8 == 0).
+  const bool tma = N % 32 == 0 && K % 8 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+  const bool pow2_group = g >= 16 && (g & (g - 1)) == 0;
+  const int path = (tma && K % kBK == 0 && g % kBK == 0) ? 0 : (tma && pow2_group) ? 1 : 2;
+#define LR_GEMM_MODE(M_)                                                                       \
+  if (path == 0) return dispatch_shape<M_>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp, \
+                                           err, stream);                                      \
+  if (path == 1) return launch_skinny<M_>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp,  \
+                                          err, stream);                                       \
+  return launch_generic<M_>(A, K, R, tab, E, mat, N, g, seg_start, seg_len, mr, Cp, err, stream)
   switch (mode) {
     case LR_FFN_MODE_PLAIN:
-      return dispatch_shape<LR_FFN_MODE_PLAIN>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr,
-                                               Cp, err, stream);
+      LR_GEMM_MODE(LR_FFN_MODE_PLAIN);
     case LR_FFN_MODE_SILU:
-      return dispatch_shape<LR_FFN_MODE_SILU>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp,
-                                              err, stream);
+      LR_GEMM_MODE(LR_FFN_MODE_SILU);
     default:
-      return dispatch_shape<LR_FFN_MODE_SWIGLU>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr,
-                                                Cp, err, stream);
+      LR_GEMM_MODE(LR_FFN_MODE_SWIGLU);
   }
+#undef LR_GEMM_MODE
 }
 
 extern "C" int lr_quantized_matmul(const void* device_table, const void* A, int M, int K, int N,
-                                   void* C, void* workspace, size_t workspace_bytes, int32_t* err,
-                                   lr_stream_t stream) {
-  return lr_grouped_w4a16_gemm(device_table, 1, LR_FFN_MODE_PLAIN, 2, A, M, K, N, nullptr,
-                               nullptr, M, C, workspace, workspace_bytes, err, stream);
+                                   int group_size, void* C, void* workspace,
+                                   size_t workspace_bytes, int32_t* err, lr_stream_t stream) {
+  return lr_grouped_w4a16_gemm(device_table, 1, LR_FFN_MODE_PLAIN, 2, A, M, K, N, group_size,
+                               nullptr, nullptr, M, C, workspace, workspace_bytes, err, stream);
 }

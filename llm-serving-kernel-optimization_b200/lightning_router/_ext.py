@@ -30,7 +30,7 @@ C_ABI_SYMBOLS = (
     "lr_combine", "lr_gather_workspace_bytes", "lr_expert_routing_gather",
     "lr_weight_table_bytes", "lr_encode_weight_table",
     "lr_grouped_gemm_workspace_bytes", "lr_grouped_w4a16_gemm", "lr_quantized_matmul",
-    "lr_ep_plan_size", "lr_ep_plan", "lr_ep_gather", "lr_ep_combine",
+    "lr_ep_plan_size", "lr_ep_plan", "lr_ep_plan_tokens", "lr_ep_gather", "lr_ep_combine",
     "lr_ipc_export", "lr_ipc_import", "lr_ipc_close",
 )
 

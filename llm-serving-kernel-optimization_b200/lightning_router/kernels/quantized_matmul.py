@@ -1,4 +1,4 @@
-"""W4A16 GEMMs on the B200 tensor cores (tcgen05).
+"""W4A16 GEMMs on the B200: tcgen05 tensor cores for the model shapes.
 
 Drop-in for the reference's ``lightning_router/kernels/quantized_matmul.py:122-173``
 (:func:`quantized_matmul`) plus the grouped expert GEMM used by ``ExpertGroup``
@@ -6,13 +6,18 @@ and ``MoELayer`` (:func:`grouped_w4a16`).
 
 Weights stay in the reference's packed format (``qweight`` (K, N/8) int32,
 ``scales`` (K/g, N) fp16, ``zeros`` (K/g, N/8) int32).  A small per-expert
-"weight table" (TMA descriptors + pointers, ~900 B per expert) is encoded once
+"weight table" (TMA descriptors + pointers, ~1.3 KB per expert) is encoded once
 per weight set and kept on the device together with references to the weight
 tensors it points to (it holds only addresses and strides, so it stays valid
 when a buffer is updated in place).  Modules keep their own tables; the
-functional :func:`quantized_matmul` uses a small bounded cache.  Limits of the tcgen05 kernel: ``K % 64 == 0``,
-``group_size % 64 == 0``, ``N % 32 == 0`` (``N % 64 == 0`` for the fused SwiGLU
-mode), at most 256 experts per launch.
+functional :func:`quantized_matmul` uses a small bounded cache.
+
+Every shape of the packed format is accepted (``K % group_size == 0``,
+``N % 8 == 0``, any M), as the reference's masked kernel does.  The kernel
+follows the shape: the tcgen05 kernel when ``K % 64 == 0``,
+``group_size % 64 == 0`` and ``N % 32 == 0``; an mma.sync kernel for
+``K % 8 == 0``, ``N % 32 == 0`` and a power-of-two group of at least 16 (e.g.
+group 32); CUDA cores otherwise (e.g. N = 48).  At most 256 experts per launch.
 """
 
 from __future__ import annotations
@@ -36,6 +41,7 @@ class WeightTable(NamedTuple):
     """
     table: torch.Tensor
     refs: tuple
+    group_size: int
 
 
 _TABLE_CACHE: "OrderedDict[tuple, WeightTable]" = OrderedDict()
@@ -62,9 +68,6 @@ def weight_table(qweights, scales, zeros, num_experts: int, d_model: int, d_ff: 
         _TABLE_CACHE.move_to_end(key)
         return hit
     dev = next(t.device for t in qweights if t is not None)
-    if group_size % 64 != 0:
-        raise NotImplementedError(
-            f"W4A16 tcgen05 kernel needs group_size % 64 == 0 (got {group_size})")
     host = _ext.ops().encode_weight_table(list(qweights), list(scales), list(zeros),
                                           int(num_experts), int(d_model), int(d_ff),
                                           int(group_size), bool(gated))
@@ -72,7 +75,7 @@ def weight_table(qweights, scales, zeros, num_experts: int, d_model: int, d_ff: 
     assert table.data_ptr() % 128 == 0
     table.copy_(host)
     refs = tuple(t for t in (*qweights, *scales, *zeros) if t is not None)
-    wt = WeightTable(table, refs)
+    wt = WeightTable(table, refs, int(group_size))
     if cache:
         _TABLE_CACHE[key] = wt
         while len(_TABLE_CACHE) > _TABLE_CACHE_MAX:
@@ -96,8 +99,8 @@ def grouped_w4a16(table: WeightTable, num_experts: int, mode: int, mat: int, A: 
     _ext.require_cuda(A)
     err = _ext.error_word(A.device.index)
     return _ext.ops().grouped_w4a16_gemm(table.table, int(num_experts), int(mode), int(mat),
-                                         A.contiguous(), int(N), seg_start, seg_len,
-                                         int(max_rows), out, err)
+                                         A.contiguous(), int(N), table.group_size, seg_start,
+                                         seg_len, int(max_rows), out, err)
 
 
 def quantized_matmul(
@@ -113,8 +116,9 @@ def quantized_matmul(
 ) -> torch.Tensor:
     """``C = A @ dequant(B)`` with A (M, K) fp16 and B packed INT4; returns (M, N) fp16.
 
-    ``block_*`` are accepted for signature compatibility and ignored: the tile
-    shape is chosen by the kernel (128 weight columns x up to 256 rows of A).
+    ``block_*`` are accepted for signature compatibility and ignored: the kernel
+    and its tile shape are chosen from the shape.  Any M; N % 8 == 0 and
+    K % group_size == 0 (the packed format's limits).
     """
     M, K = A.shape
     assert A.dtype == torch.float16
@@ -122,8 +126,11 @@ def quantized_matmul(
     _ext.require_cuda(A, B_packed, scales, zeros)
     if B_packed.shape != (K, N // 8):
         raise ValueError(f"B_packed shape {tuple(B_packed.shape)} != ({K}, {N // 8})")
-    if K % 64 != 0 or N % 32 != 0:
-        raise NotImplementedError(f"W4A16 kernel needs K % 64 == 0 and N % 32 == 0 (K={K}, N={N})")
+    if N % 8 != 0 or group_size < 1 or K % group_size != 0:
+        raise ValueError(f"packed INT4 needs N % 8 == 0 and K % group_size == 0 "
+                         f"(K={K}, N={N}, group_size={group_size})")
+    if scales.shape != (K // group_size, N) or zeros.shape != (K // group_size, N // 8):
+        raise ValueError("scales / zeros shapes do not match (K / group_size, N) / (K / group_size, N / 8)")
     if M == 0:
         return torch.empty(0, N, dtype=torch.float16, device=A.device)
     # cache only tables over the caller's own tensors, never over temporaries

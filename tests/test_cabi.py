@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = _ext.clib()
-    assert lib.lr_abi_version() == 1
+    assert lib.lr_abi_version() == 2
     assert lib.lr_status_string(0) == b"ok"
     assert b"invalid" in lib.lr_status_string(-1)
     assert b"workspace" in lib.lr_status_string(-4)
@@ -68,9 +68,13 @@ def test_argument_validation_without_device():
         assert lib.lr_gate_topk_gating_dispatch(
             None, None, None, T, d, E, k, 8, ctypes.c_float(0.01), 0, None, *nulls,
             None, ctypes.c_size_t(0), None, None) == -1
-    # K not a multiple of 64
-    assert lib.lr_grouped_w4a16_gemm(ctypes.c_void_p(128), 1, 0, 2, None, 4, 100, 64, None, None,
-                                     4, None, None, ctypes.c_size_t(0), None, None) in (-1, -2)
+    # group size not dividing K, N not a multiple of 8, no operands
+    for K, N, g in [(100, 64, 64), (128, 60, 64), (128, 64, 0)]:
+        assert lib.lr_grouped_w4a16_gemm(ctypes.c_void_p(128), 1, 0, 2, None, 4, K, N, g, None,
+                                         None, 4, None, None, ctypes.c_size_t(0), None,
+                                         None) in (-1, -2)
+    assert lib.lr_grouped_w4a16_gemm(ctypes.c_void_p(128), 1, 0, 2, None, 4, 96, 48, 32, None,
+                                     None, 4, None, None, ctypes.c_size_t(0), None, None) == -1
 
 
 def test_torch_ops_register():

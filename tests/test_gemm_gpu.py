@@ -60,6 +60,58 @@ def test_quantized_matmul_shapes(M, K, N, g):
     _check(C, A.float() @ Wd.float())
 
 
+@pytest.mark.parametrize("M,K,N,g", [
+    # the reference's own shapes (tests/test_quantization.py:61-93)
+    (32, 256, 64, 128), (64, 256, 64, 128),
+    # group 32 / K % 64 != 0: the mma.sync kernel (one and several 32-row token tiles)
+    (32, 256, 64, 32), (7, 96, 64, 32), (300, 128, 256, 32), (17, 1024, 1408, 32),
+    (64, 200, 96, 8 * 5),
+    # N % 32 != 0, groups of 8 or 24, K % 8 != 0: CUDA cores
+    (7, 96, 48, 32), (100, 256, 48, 128), (64, 40, 64, 8), (5, 72, 32, 24), (9, 36, 24, 12),
+])
+def test_quantized_matmul_any_packed_shape(M, K, N, g):
+    """Every shape the packed format admits (K % g == 0, N % 8 == 0, any M), as the
+    reference's masked Triton kernel accepts, against dequantize + fp32 matmul."""
+    from lightning_router.kernels.quantized_matmul import quantized_matmul
+    qw, s, z, Wd = _quant(K, N, g, 7 * M + K + N + g)
+    A = torch.randn(M, K, device=DEV).half()
+    C = quantized_matmul(A, qw, s, z, N=N, group_size=g)
+    assert C.shape == (M, N)
+    _check(C, A.float() @ Wd.float())
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("d,f,g", [(96, 48, 16), (256, 96, 32), (128, 64, 64)])
+def test_grouped_modes_off_tcgen05_shapes(mode, d, f, g):
+    """Grouped modes where gate/up and down take different kernels (CUDA cores for
+    N = 48, mma.sync for group 16/32), with ragged and empty segments."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E = 4
+    lens = [5, 0, 40, 17]
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, mode, seed=300 + d + f + g + mode)
+    for mat, (K, N) in ((1, (d, f)), (2, (f, d))):
+        if mat == 2 and mode == 2:
+            continue  # SwiGLU is a gate/up launch
+        X = A if K == d else torch.randn(R, K, device=DEV).half()
+        sentinel = torch.full((R, N), 3.0, dtype=torch.float16, device=DEV)
+        out = grouped_w4a16(table, E, mode, mat, X, N, ss, sl, max(lens), out=sentinel.clone())
+        covered = torch.zeros(R, dtype=torch.bool, device=DEV)
+        for e, L in enumerate(lens):
+            st = int(ss[e])
+            if L == 0:
+                continue
+            x = X[st:st + L].float()
+            if mode == 0:
+                ref = x @ deq[e][mat].float()
+            elif mode == 1:
+                ref = torch.nn.functional.silu(x @ deq[e][mat].float())
+            else:
+                ref = torch.nn.functional.silu(x @ deq[e][0].float()) * (x @ deq[e][1].float())
+            _check(out[st:st + L], ref)
+            covered[st:st + L] = True
+        assert torch.equal(out[~covered], sentinel[~covered])
+
+
 @pytest.mark.parametrize("name", ["m1", "m2"])
 def test_matches_reference_triton_fixture(name):
     from lightning_router.kernels.quantized_matmul import quantized_matmul

@@ -77,6 +77,10 @@ def test_pr1_layer_matches_oracle():
     ("fine", dict(tokens=1024, d_model=512)),
     ("prefill", dict(tokens=2048, d_model=512, d_ff=1024)),
     ("pr1", dict(tokens=333, capacity_factor=0.5)),
+    # shapes off the tcgen05 kernel: group 32 (mma.sync kernel), N = 48 / group 16
+    # (up projection on CUDA cores, down projection on mma.sync)
+    ("decode", dict(d_model=256, d_ff=512, group_size=32)),
+    ("pr1", dict(tokens=300, d_model=96, d_ff=48, group_size=16)),
 ])
 def test_reduced_layers_match_oracle(name, overrides):
     from lightning_router.workloads import WORKLOADS
