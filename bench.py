@@ -14,11 +14,16 @@ value     MoE-layer tokens/s of the whole job, device-timed (CUDA events, max ov
           inputs resident in HBM.
 e2e       the same metric through ``MoELayer.forward`` with the input copied from pinned
           host memory and the output read back every step.
-roofline  the dominant kernel (grouped W4A16 gate/up GEMM): algorithmic FLOPs per launch /
-          its CUDA-event duration inside the timed steps, against the measured sustained
-          bf16 tensor peak.
-cpu_baseline  the CPU oracle (numpy fp32 restatement of the reference path) on the host
-          cores, rank 0 only, on a bounded token sample.
+roofline  the dominant kernel (grouped W4A16 gate/up GEMM), device-timed inside the timed
+          steps.  Compute-bound workloads (prefill, pr1, fine): algorithmic FLOPs per launch
+          against the measured bf16 tensor peak -- the burst figure when the sampled SM clock
+          stayed at its maximum, the sustained (power-capped) one otherwise; both fractions are
+          printed.  Weight-stream-bound workloads (decode): algorithmic bytes per launch (the
+          packed weights, scales and zeros of every expert with a kept row, plus activation
+          rows in and out) against the measured HBM copy bandwidth.
+cpu_baseline  the reference's own CPU path (its torch-routing MoELayer in fp32, restated
+          in oracle/torch_path.py and pinned against the reference's outputs) on every host
+          thread, rank 0 only, on a bounded token sample (about 10 s of work).
 
 ``--impl reference`` times that CPU implementation alone on the same workload and
 prints its line with ``"impl": "reference"``.
@@ -47,13 +52,14 @@ import torch  # noqa: E402
 METRIC = "MoE-layer tokens/s"
 UNIT = "tokens/s"
 
-# DRAM bytes (read + write) per launch of the dominant kernel (the gate/up GEMM)
-# from full-size ncu captures of the bench's own timed steps, keyed by workload
-# (profiles/launches_prefill16k.md, profiles/launches_decode64.md); None until
-# captured.
+# DRAM bytes (read + write) per launch of the dominant kernel (the gate/up GEMM),
+# from one ncu capture of this bench's own command per workload:
+#   ncu --clock-control none --metrics dram__bytes_read.sum,dram__bytes_write.sum \
+#       -k regex:w4a16 -c 2 python bench.py --workload W --steps 2 --warmup 3 --no-cpu
+# (the first launch of each GEMM); None until captured for the current kernels.
 NCU_TRAFFIC = {
-    "prefill": 809.0e6 + 907.3e6,   # rows in 268 MB + weights 487 MB, rows out 940 MB
-    "decode": 489.8e6 + 2.6e6,      # weights 487 MB
+    "prefill": None,
+    "decode": None,
 }
 
 
@@ -153,60 +159,63 @@ def max_over_ranks(v: float, ws: int) -> float:
 # ---------------------------------------------------------------------------
 # CPU oracle timing (baseline / reference arm)
 # ---------------------------------------------------------------------------
-def cpu_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
-
-
-def cpu_oracle_setup(w, sample_tokens: int):
-    """Dequantized fp32 expert weights on the host (untimed load) and a token sample."""
-    import oracle as orc  # the CPU restatement, used here as the timed baseline
+def cpu_port_setup(w):
+    """fp32 inputs of the CPU baseline (untimed): dequantized INT4 experts, gate weight,
+    gate bias and the workload's tokens, on the host."""
     from lightning_router.quantization.pack_weights import dequantize_tensor
     from lightning_router.workloads import make_layer
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    t = make_layer(w, device=dev, gen_device=dev, tokens=sample_tokens)
-    experts = []
-    for ex in t.experts:
-        experts.append({n: dequantize_tensor(q, s, z, w.group_size, s.shape[1]).float().cpu().numpy()
-                        for n, (q, s, z) in ex.items()})
-    x = t.x.cpu().numpy()
-    wg = t.gate_w.cpu().numpy()
-    bias = None if t.bias is None else t.bias.cpu().numpy()
+    t = make_layer(w, device=dev, gen_device=dev)
+    experts = [{n: dequantize_tensor(q, s, z, w.group_size, s.shape[1]).float().cpu()
+                for n, (q, s, z) in ex.items()} for ex in t.experts]
+    x = t.x.float().cpu()
+    wg = t.gate_w.float().cpu()
+    bias = None if t.bias is None else t.bias.float().cpu()
     del t
     if dev == "cuda":
         torch.cuda.empty_cache()
-    return orc, x, wg, bias, experts
+    return x, wg, bias, experts
 
 
-def cpu_oracle_step(orc, w, x, wg, bias, experts):
-    logits = orc.gate_logits(x, wg, bias)
-    out, aux, _ = orc.moe_layer(x, logits, w.top_k, w.capacity_factor, experts)
-    return out
+def cpu_port_step(w, x, wg, bias, experts):
+    # the reference's torch-routing MoELayer restated (the timed baseline, not the product)
+    from oracle import torch_path
+    return torch_path.moe_layer(x, wg, experts, w.top_k, gated=w.activation == "swiglu",
+                                bias=bias)
 
 
-def run_cpu(w, steps: int, warmup: int, budget_s: float = 20.0):
-    """Times the CPU oracle; returns (tokens/s, sample description, threads)."""
-    sample = min(w.tokens, 512 if w.d_ff >= 8192 else 1024)
-    orc, x, wg, bias, experts = cpu_oracle_setup(w, sample)
-    for _ in range(max(0, warmup)):
-        cpu_oracle_step(orc, w, x, wg, bias, experts)
-    n, t0 = 0, time.perf_counter()
-    while n < max(1, steps):
-        cpu_oracle_step(orc, w, x, wg, bias, experts)
-        n += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = time.perf_counter() - t0
-    desc = (f"{n} step(s) of {sample} of {w.tokens} tokens through the numpy fp32 oracle "
-            f"(gate, top-k, capacity {w.capacity_factor}, dequantized INT4 experts, combine); "
-            f"weights dequantized once outside the timed region")
-    return sample * n / dt, desc, cpu_threads()
+def run_cpu(w, steps: int, warmup: int, step_budget_s: float = 10.0):
+    """Times the reference's CPU path (its torch-routing MoELayer in fp32, restated in
+    ``oracle/torch_path.py``) with every host thread; returns (tokens/s, sample, threads).
+
+    Each step runs the first ``sample`` tokens of the workload, ``sample`` sized by an
+    untimed calibration step so that one step takes about ``step_budget_s`` seconds
+    (at most the whole workload).  The torch path applies no capacity, so the work
+    per token does not depend on the sample size.
+    """
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    with torch.no_grad():
+        x, wg, bias, experts = cpu_port_setup(w)
+        n0 = min(w.tokens, 256)
+        t0 = time.perf_counter()
+        cpu_port_step(w, x[:n0], wg, bias, experts)
+        rate = n0 / max(time.perf_counter() - t0, 1e-9)
+        sample = int(min(w.tokens, max(n0, rate * step_budget_s)))
+        sample = max(n0, sample - sample % 64) if sample < w.tokens else w.tokens
+        xs = x[:sample].contiguous()
+        for _ in range(max(0, warmup)):
+            cpu_port_step(w, xs, wg, bias, experts)
+        t0 = time.perf_counter()
+        for _ in range(max(1, steps)):
+            cpu_port_step(w, xs, wg, bias, experts)
+        dt = time.perf_counter() - t0
+    n = max(1, steps)
+    desc = (f"{n} step(s) of the first {sample} of {w.tokens} tokens through the reference's "
+            f"torch-routing MoELayer path restated in fp32 (gate, softmax, top-k, per-expert "
+            f"mask + index_add_, dequantized INT4 experts as fp32 matmuls, no capacity), "
+            f"torch on {threads} host threads; weights dequantized outside the timed region")
+    return sample * n / dt, desc, threads
 
 
 # ---------------------------------------------------------------------------
@@ -233,6 +242,59 @@ def stage_times(events, steps):
             acc.setdefault(name, []).append(prev.elapsed_time(ev))
         prev = ev
     return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
+def gemm_roofline(w, layer, model, x, st, clk, peaks, peak_kind, workload, ws, rank):
+    """Roofline of the dominant kernel, the grouped gate/up GEMM (its stage time).
+
+    Per launch: FLOPs = 2 * kept rows * (2 if SwiGLU else 1) * d_model * d_ff;
+    algorithmic bytes = packed weights + scales + zeros of every local expert with a
+    kept row + kept rows in (d_model fp16) and out (d_ff fp16).  The bound is the
+    one whose roof is lower at that arithmetic intensity.
+    """
+    gated = w.activation == "swiglu"
+    if hasattr(model, "last_kept_per_expert"):
+        kept_e = model.last_kept_per_expert()
+    else:
+        _, plan = layer.route(x)
+        kept_e = plan.kept_counts.cpu().tolist()
+    kept = int(sum(kept_e))
+    nmat = 2 if gated else 1
+    d, f, g = w.d_model, w.d_ff, w.group_size
+    per_expert = nmat * (d * f // 2 + (d // g) * f * 2 + (d // g) * (f // 8) * 4)
+    gemm_bytes = sum(per_expert for c in kept_e if c) + kept * (d + f) * 2
+    gemm_flops = 2 * kept * nmat * d * f
+    gemm_ms = st.get("ffn_in")
+    burst = float(peaks.get("bf16_tflops"))
+    sustained = float(peaks.get("bf16_tflops_sustained", burst))
+    hbm = float(peaks["hbm_gbs"])
+    sm, smax = clk.get("sm_mhz"), clk.get("sm_max_mhz")
+    at_max = sm is not None and smax and sm >= 0.95 * smax
+    tensor_peak = burst if at_max or sm is None else sustained
+    hbm_bound = gemm_flops / max(gemm_bytes, 1) < tensor_peak * 1e12 / (hbm * 1e9)
+    out = {"kernel": "w4a16 grouped GEMM, gate/up (" + ("SwiGLU" if gated else "SiLU") +
+                     " epilogue)",
+           "launch_ms": gemm_ms, "flops_per_launch": gemm_flops,
+           "bytes_per_launch": gemm_bytes,
+           "traffic": NCU_TRAFFIC.get(workload) if ws == 1 else None,
+           "stage_ms": {k: round(v, 4) for k, v in st.items()}}
+    if not gemm_ms:
+        return {"bound": "hbm" if hbm_bound else "tensor", "achieved": None, **out}
+    tflops = gemm_flops / (gemm_ms / 1e3) / 1e12
+    gbs = gemm_bytes / (gemm_ms / 1e3) / 1e9
+    if hbm_bound:
+        out.update({"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                    "frac": gbs / hbm, "peak_kind": f"{peak_kind} HBM copy bandwidth",
+                    "tflops": tflops})
+    else:
+        out.update({"bound": "tensor", "achieved": tflops, "peak": tensor_peak,
+                    "unit": "TFLOP/s", "frac": tflops / tensor_peak,
+                    "peak_kind": (f"{peak_kind} bf16 " + ("burst" if tensor_peak == burst
+                                                          else "sustained") +
+                                  f" (median SM clock {sm} of {smax} MHz)"),
+                    "frac_burst": tflops / burst, "frac_sustained": tflops / sustained,
+                    "gbs": gbs})
+    return out
 
 
 def run_gpu(args, ws, rank, local):
@@ -334,26 +396,8 @@ def run_gpu(args, ws, rank, local):
     stage_owner.stage_events = None
     value = w.tokens * args.steps / (ms / 1e3)
 
-    # dominant kernel roofline: grouped gate/up GEMM (2/3 of the FFN FLOPs for SwiGLU)
-    plan_kept = model.last_kept_rows() if hasattr(model, "last_kept_rows") else None
-    if plan_kept is None:
-        _, plan = layer.route(x)
-        plan_kept = int(plan.kept_counts.sum())
-    gated = w.activation == "swiglu"
-    gemm_in_flops = 2 * plan_kept * (2 if gated else 1) * w.d_model * w.d_ff
-    gemm_ms = st.get("ffn_in")
-    achieved = gemm_in_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None
-    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    roofline = {
-        "kernel": "w4a16_grouped_gemm (gate/up, SwiGLU epilogue)",
-        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-        "frac": (achieved / peak) if achieved else None,
-        "peak_kind": f"{peak_kind} sustained bf16",
-        "traffic": NCU_TRAFFIC.get(args.workload),
-        "flops_per_launch": gemm_in_flops,
-        "launch_ms": gemm_ms,
-        "stage_ms": {k: round(v, 4) for k, v in st.items()},
-    }
+    roofline = gemm_roofline(w, layer, model, x, st, clk, peaks, peak_kind, args.workload, ws,
+                             rank)
 
     # end to end through the public API with host buffers (pinned), max over ranks: every
     # step copies its input from pinned host memory and its output back, through the
@@ -406,7 +450,7 @@ def run_gpu(args, ws, rank, local):
         "wall_s_timed": wall,
     }
     if ws == 1 and rank == 0 and not args.no_cpu:
-        v, desc, cores = run_cpu(w, steps=2, warmup=0)
+        v, desc, cores = run_cpu(w, steps=1, warmup=0)
         result["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                                   "sample": desc}
     return result
@@ -482,8 +526,10 @@ def run_reference(args, ws, rank):
     w = WORKLOADS["prefill" if args.workload == "sweep" else args.workload]
     if rank != 0:
         return None
-    v, desc, cores = run_cpu(w, steps=max(1, args.steps), warmup=min(args.warmup, 1),
-                             budget_s=60.0)
+    # the whole --steps/--warmup run stays within about three minutes
+    per_step = min(10.0, 180.0 / max(1, args.steps + args.warmup))
+    v, desc, cores = run_cpu(w, steps=max(1, args.steps), warmup=args.warmup,
+                             step_budget_s=per_step)
     return {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,

@@ -107,3 +107,45 @@ def test_layer_matches_reference_torch_path(name):
     ref = z[f"{name}_out"].reshape(-1, d)
     np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-5)
     assert abs(aux - float(z[f"{name}_aux"])) <= 1e-5 * abs(float(z[f"{name}_aux"]))
+
+
+@pytest.mark.parametrize("name", ["l4", "l8"])
+def test_torch_path_port_matches_reference_layer(name):
+    """The timed CPU baseline (a port of the reference's torch-routing MoELayer)
+    reproduces the reference's own outputs and aux loss on its fixture."""
+    import torch
+
+    from oracle import torch_path
+    z = golden("layer_torch")
+    B, Sq, d, f, E, k, gs = (int(v) for v in z[f"{name}_dims"])
+    experts = []
+    for e in range(E):
+        ex = {}
+        for m in ("gate", "up", "down"):
+            N = f if m != "down" else d
+            ex[m] = torch.from_numpy(orc.dequantize_tensor(
+                z[f"{name}_e{e}_{m}_qweight"], z[f"{name}_e{e}_{m}_scales"],
+                z[f"{name}_e{e}_{m}_zeros"], gs, N).astype(np.float32))
+        experts.append(ex)
+    x = torch.from_numpy(z[f"{name}_x"]).reshape(-1, d)
+    wg = torch.from_numpy(z[f"{name}_wg"])
+    out, aux = torch_path.moe_layer(x, wg, experts, k)
+    ref = z[f"{name}_out"].reshape(-1, d)
+    np.testing.assert_allclose(out.numpy(), ref, rtol=1e-5, atol=1e-6)
+    assert abs(float(aux) - float(z[f"{name}_aux"])) <= 1e-6 * abs(float(z[f"{name}_aux"]))
+
+
+def test_vectorized_routing_port_is_weighted_identity():
+    """Identity experts: the sweep baseline returns sum_j w_j * x_t per token."""
+    import torch
+
+    from oracle import torch_path
+    g = torch.Generator().manual_seed(5)
+    T, d, E, k = 37, 16, 4, 2
+    x = torch.randn(T, d, generator=g).half()
+    ids, w, _ = orc.topk_gating(torch.randn(T, E, generator=g).numpy(), k)
+    ids, w = torch.from_numpy(ids.reshape(-1)).long(), torch.from_numpy(w.reshape(-1))
+    tok = torch.arange(T).repeat_interleave(k)
+    out = torch_path.vectorized_routing(x, ids, w, tok, E)
+    ref = (x.float() * w.view(T, k).sum(1, keepdim=True)).half()
+    assert torch.allclose(out.float(), ref.float(), atol=2e-3)
