@@ -39,6 +39,7 @@ typedef struct CUstream_st* lr_stream_t; /* == cudaStream_t */
 #define LR_DEVERR_BAD_TOKEN 0x2      /* a source token outside [0, T) */
 #define LR_DEVERR_PIPE_TIMEOUT 0x4   /* a GEMM pipeline wait ran out of time */
 #define LR_DEVERR_BAD_SEGMENT 0x8    /* a GEMM row segment outside the row range */
+#define LR_DEVERR_PEER_TIMEOUT 0x10  /* another rank's exchange flag did not arrive in time */
 
 const char* lr_status_string(int status);
 int lr_abi_version(void);
@@ -236,14 +237,18 @@ int lr_quantized_matmul(const void* device_table, const void* A, int M, int K, i
 /* ---- expert-parallel exchange over NVLink peer memory --------------------
  * Replaces the all-GPU expert execution + host all-reduce of the reference's
  * serving worker (lightning_router/serving/worker.py:156-186) for one process
- * per GPU.  Rank r owns experts [r*E/G, (r+1)*E/G).  The caller keeps three
+ * per GPU.  Rank r owns experts [r*E/G, (r+1)*E/G).  The caller keeps five
  * buffers per rank mapped by every other rank (lr_ipc_*): the rank's tokens,
  * the row -> token map of its uncapped expert segments (source_idx of
- * lr_permute_tokens without rows) and the expert-output rows it computes;
- * peer_* are device arrays of the G ranks' addresses of such a buffer.
- * Ordering across GPUs is the caller's: a collective after the tokens and
- * maps are written (the counts all-gather) before lr_ep_gather, and one after
- * the expert outputs are written before lr_ep_combine.                       */
+ * lr_permute_tokens without rows), the expert-output rows it computes, a
+ * statistics table (G rows of 1 + 2E doubles) and 2G int32 flags (zeroed
+ * once); peer_* are device arrays of the G ranks' addresses of such a buffer.
+ * A step is: lr_ep_publish -> lr_ep_plan_wait -> lr_ep_gather -> expert GEMMs
+ * -> lr_ep_signal -> lr_ep_combine, with `epoch` = 1, 2, ... the step number
+ * (the same on every rank).  The flags order every cross-GPU read after the
+ * matching writes and every overwrite after the matching reads; each wait is
+ * bounded (LR_DEVERR_PEER_TIMEOUT).  lr_ep_plan / lr_ep_plan_tokens plan from
+ * counts the caller gathered itself (an NCCL exchange).                      */
 
 /* Number of int32 entries of an exchange plan. */
 int lr_ep_plan_size(int world, int num_experts);
@@ -267,6 +272,28 @@ int lr_ep_plan_tokens(const int32_t* counts, const int32_t* shard_tokens, int wo
                       int num_experts, int top_k, double capacity_factor, int rank,
                       int max_capacity, int32_t* plan, int32_t* err, lr_stream_t stream);
 
+/* Writes this rank's statistics row (num_tokens, per-expert counts from the
+ * CSR offsets, per-expert probability sums; zeros when num_tokens == 0) into
+ * slot `rank` of every rank's table, then raises its stats flag (flags[rank])
+ * on every rank with the value epoch.                                        */
+int lr_ep_publish(const uint64_t* peer_stats, const uint64_t* peer_flags, const int32_t* offsets,
+                  const double* prob_sums, int num_tokens, int world, int num_experts, int rank,
+                  int epoch, lr_stream_t stream);
+
+/* Waits (bounded) until every rank's stats flag reached epoch, then plans as
+ * lr_ep_plan_tokens from the table (capacity from the summed token counts,
+ * clipped to max_capacity) and writes the whole job's auxiliary loss
+ * (reference lightning_router/models/gating.py:91-99).  A flag that does not
+ * arrive sets LR_DEVERR_PEER_TIMEOUT and yields a plan that keeps no rows.   */
+int lr_ep_plan_wait(const double* stats, const int32_t* flags, int world, int num_experts,
+                    int rank, int top_k, double capacity_factor, int max_capacity,
+                    float load_balance_weight, int epoch, int32_t* plan, float* aux_loss,
+                    int32_t* err, lr_stream_t stream);
+
+/* After this rank's expert GEMMs: raises its outputs flag (flags[G + rank]) on
+ * every rank with the value epoch.                                           */
+int lr_ep_signal(const uint64_t* peer_flags, int world, int rank, int epoch, lr_stream_t stream);
+
 /* Expert owner: rows of its segments <- the kept token rows, read from the
  * source ranks' token buffers (tokens < max_tokens, map entries < max_slots).
  * out has rows_max = E/G * capacity rows of d fp16; rows past the segments are
@@ -278,11 +305,13 @@ int lr_ep_gather(const uint64_t* peer_tokens, const uint64_t* peer_source_idx,
 
 /* Token owner: out[t,:] = fp16( sum_j gate_weights[t*k+j] * y_owner[row, :] )
  * over the kept slots in slot order (fp32), y read from the owners' expert
- * output buffers; slot_pos holds each slot's uncapped local row.             */
+ * output buffers; slot_pos holds each slot's uncapped local row.  With
+ * ready_flags (this rank's flags + G) it first waits (bounded) until every
+ * rank's outputs flag reached epoch; without, the caller orders the reads.   */
 int lr_ep_combine(const uint64_t* peer_outputs, const int32_t* plan, const int32_t* expert_ids,
                   const float* gate_weights, const int32_t* slot_pos, int T, int k, int world,
-                  int num_experts, int d, int rows_max, void* out, int32_t* err,
-                  lr_stream_t stream);
+                  int num_experts, int d, int rows_max, void* out, const int32_t* ready_flags,
+                  int epoch, int32_t* err, lr_stream_t stream);
 
 /* CUDA IPC of a device buffer: export writes a 64-byte handle of the buffer's
  * allocation and the buffer's offset in it; import (in another process) maps

@@ -15,9 +15,22 @@
 //   * lr_ep_combine (token owner) pulls each kept slot's expert output row from
 //     the expert owner and sums them in slot order in fp32, exactly as the
 //     single-GPU combine.
-// Cross-rank ordering comes from the caller's stream-ordered collectives (the
-// counts all-gather after the buffers are written, and one more small
-// collective after the expert GEMMs); these kernels never wait on another GPU.
+// Cross-rank ordering needs no collective library call in the step: flags in
+// the mapped memory, written with release and read with acquire semantics at
+// system scope, with every wait bounded in time (LR_DEVERR_PEER_TIMEOUT):
+//   * lr_ep_publish writes this rank's statistics row (token count, per-expert
+//     counts and probability sums) into every rank's table and raises its
+//     "stats" flag there; lr_ep_plan_wait waits for every rank's flag of the
+//     step, then plans and computes the auxiliary loss;
+//   * lr_ep_signal raises this rank's "outputs" flag on every rank after its
+//     expert GEMMs; lr_ep_combine waits for every rank's flag before it reads.
+// Flags hold the step number (the epoch), so nothing is reset between steps.
+// A rank overwrites its token and row-map buffers only after its combine saw
+// every owner's outputs flag (so every owner's gather of the previous step is
+// done), and an owner overwrites its outputs only after its plan saw every
+// rank's stats flag of the next step (so every combine of the previous step is
+// done).  Publish and wait are separate launches, so ranks emulated one after
+// the other on one GPU never wait on a later launch.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -46,48 +59,14 @@ struct EpPlanLayout {
   }
 };
 
-// One block.  counts[r*E + e] = slots of expert e on rank r (uncapped, in the
-// rank's slot order).  Rank r's slots of e follow those of lower ranks in the
-// global slot order, so kept(r, e) = clamp(C - sum_{r' < r} counts[r'][e], 0,
-// counts[r][e]) -- the single-GPU capacity rule.  With shard_tokens (the G
-// ranks' token counts) C is max(int((k * sum T_r / E) * cf), 1) in double
-// precision, as on one GPU (reference kernels/expert_routing.py:196-197), and
-// capacity is the largest C the caller's buffers hold; otherwise C = capacity.
-__global__ void __launch_bounds__(256)
-    ep_plan_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ shard_tokens,
-                   int G, int E, int top_k, double cf, int rank, int capacity,
-                   int32_t* __restrict__ plan, int32_t* err) {
-  __shared__ int s_cnt[kEpMaxCounts];
-  __shared__ int s_kept[kEpMaxCounts];
-  __shared__ int s_cap;
+// Plan of one rank, one block, from s_cnt[r*E + e] = slots of expert e on rank r
+// (uncapped, in the rank's slot order) and the capacity C.  Rank r's slots of e
+// follow those of lower ranks in the global slot order, so kept(r, e) =
+// clamp(C - sum_{r' < r} counts[r'][e], 0, counts[r][e]) -- the single-GPU
+// capacity rule.
+LR_DEVICE void ep_plan_block(const int* s_cnt, int* s_kept, int G, int E, int rank, int C,
+                             int32_t* __restrict__ plan) {
   const EpPlanLayout L(G, E);
-  for (int i = threadIdx.x; i < G * E; i += blockDim.x) {
-    int c = counts[i];
-    if (c < 0) {
-      report(err, LR_DEVERR_BAD_SEGMENT);
-      c = 0;
-    }
-    s_cnt[i] = c;
-  }
-  if (threadIdx.x == 0) {
-    int C = capacity;
-    if (shard_tokens) {
-      long long T = 0;
-      for (int r = 0; r < G; ++r) {
-        const int t = shard_tokens[r];
-        if (t < 0) report(err, LR_DEVERR_BAD_SEGMENT);
-        else T += t;
-      }
-      const double q = double(T * top_k) / double(E);
-      const long long c = (long long)(q * cf);
-      C = c < 1 ? 1 : (c > capacity ? capacity : int(c));
-      if (c > capacity) report(err, LR_DEVERR_BAD_SEGMENT);  // buffers too small: rows clipped
-    }
-    s_cap = C;
-    plan[L.cap] = C;
-  }
-  __syncthreads();
-  const int C = s_cap;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int base = 0;
     for (int r = 0; r < G; ++r) {
@@ -99,6 +78,7 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
+  plan[L.cap] = C;
   const int El = L.El;
   // owner side: segments [local expert][source rank]
   int row = 0;
@@ -131,6 +111,150 @@ __global__ void __launch_bounds__(256)
     for (int r = 0; r < rank; ++r) start += s_kept[r * E + e];
     plan[L.dst_row + e] = start;
   }
+}
+
+// C = max(int((k * T / E) * cf), 1) in double precision, as on one GPU
+// (reference kernels/expert_routing.py:196-197), clipped to the buffers' bound.
+LR_DEVICE int ep_capacity(long long T, int top_k, int E, double cf, int cap_max, int32_t* err) {
+  const double q = double(T * top_k) / double(E);
+  const long long c = (long long)(q * cf);
+  if (c > cap_max) report(err, LR_DEVERR_BAD_SEGMENT);  // buffers too small: rows clipped
+  return c < 1 ? 1 : (c > cap_max ? cap_max : int(c));
+}
+
+// One block.  counts[r*E + e] from the caller.  With shard_tokens (the G ranks'
+// token counts) the capacity is computed as on one GPU, `capacity` being the
+// largest C the caller's buffers hold; otherwise C = capacity.
+__global__ void __launch_bounds__(256)
+    ep_plan_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ shard_tokens,
+                   int G, int E, int top_k, double cf, int rank, int capacity,
+                   int32_t* __restrict__ plan, int32_t* err) {
+  __shared__ int s_cnt[kEpMaxCounts];
+  __shared__ int s_kept[kEpMaxCounts];
+  __shared__ int s_cap;
+  for (int i = threadIdx.x; i < G * E; i += blockDim.x) {
+    int c = counts[i];
+    if (c < 0) {
+      report(err, LR_DEVERR_BAD_SEGMENT);
+      c = 0;
+    }
+    s_cnt[i] = c;
+  }
+  if (threadIdx.x == 0) {
+    int C = capacity;
+    if (shard_tokens) {
+      long long T = 0;
+      for (int r = 0; r < G; ++r) {
+        const int t = shard_tokens[r];
+        if (t < 0) report(err, LR_DEVERR_BAD_SEGMENT);
+        else T += t;
+      }
+      C = ep_capacity(T, top_k, E, cf, capacity, err);
+    }
+    s_cap = C;
+  }
+  __syncthreads();
+  ep_plan_block(s_cnt, s_kept, G, E, rank, s_cap, plan);
+}
+
+LR_DEVICE void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+LR_DEVICE int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr uint64_t kPeerWaitNs = 5000000000ull;  // 5 s: a rank that far behind has failed
+
+// Waits until flags[i] >= epoch for i < n; false (and LR_DEVERR_PEER_TIMEOUT) when
+// one has not arrived within kPeerWaitNs.
+LR_DEVICE bool wait_flags(const int32_t* flags, int n, int epoch, int32_t* err) {
+  const uint64_t t0 = global_timer_ns();
+  for (int i = 0; i < n; ++i) {
+    while (ld_acquire_sys(flags + i) < epoch) {
+      if (global_timer_ns() - t0 > kPeerWaitNs) {
+        report(err, LR_DEVERR_PEER_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// This rank's statistics row [T, count[0..E), prob_sum[0..E)] (doubles) into
+// slot `rank` of every rank's table, then this rank's stats flag on every rank.
+__global__ void __launch_bounds__(256)
+    ep_publish_kernel(const uint64_t* __restrict__ peer_stats,
+                      const uint64_t* __restrict__ peer_flags, const int32_t* __restrict__ offsets,
+                      const double* __restrict__ prob_sums, int T_l, int G, int E, int rank,
+                      int epoch) {
+  const int W = 1 + 2 * E;
+  for (int i = threadIdx.x; i < G * W; i += blockDim.x) {
+    const int q = i / W, j = i % W;
+    double v = 0.0;
+    if (j == 0) v = double(T_l);
+    else if (offsets && j <= E) v = double(offsets[j] - offsets[j - 1]);
+    else if (prob_sums && j > E) v = prob_sums[j - 1 - E];
+    reinterpret_cast<double*>(peer_stats[q])[rank * W + j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < G; ++q) st_release_sys(reinterpret_cast<int32_t*>(peer_flags[q]) + rank, epoch);
+  }
+}
+
+// Waits for every rank's stats row of step `epoch` in this rank's table, then
+// plans (ep_plan_block) and writes the auxiliary loss of the whole job,
+// lbw * E * sum_e f_e P_e with f_e = count_e / (k T), P_e = prob_sum_e / T
+// (reference lightning_router/models/gating.py:91-99).  When a flag does not
+// arrive the plan keeps no rows.
+__global__ void __launch_bounds__(256)
+    ep_plan_wait_kernel(const double* __restrict__ stats, const int32_t* __restrict__ flags,
+                        int G, int E, int rank, int top_k, double cf, int cap_max, float lbw,
+                        int epoch, int32_t* __restrict__ plan, float* __restrict__ aux,
+                        int32_t* err) {
+  __shared__ int s_cnt[kEpMaxCounts];
+  __shared__ int s_kept[kEpMaxCounts];
+  __shared__ int s_ok, s_cap;
+  if (threadIdx.x == 0) s_ok = wait_flags(flags, G, epoch, err) ? 1 : 0;
+  __syncthreads();
+  const int W = 1 + 2 * E;
+  for (int i = threadIdx.x; i < G * E; i += blockDim.x) {
+    const int r = i / E, e = i % E;
+    const double c = s_ok ? __ldcv(stats + r * W + 1 + e) : 0.0;
+    s_cnt[i] = c > 0.0 ? int(c + 0.5) : 0;
+  }
+  if (threadIdx.x == 0) {
+    double T = 0.0;
+    for (int r = 0; r < G; ++r) T += s_ok ? __ldcv(stats + r * W) : 0.0;
+    s_cap = ep_capacity((long long)(T + 0.5), top_k, E, cf, cap_max, err);
+    double a = 0.0;
+    if (s_ok && T > 0.0) {
+      for (int e = 0; e < E; ++e) {
+        double cnt = 0.0, ps = 0.0;
+        for (int r = 0; r < G; ++r) {
+          cnt += __ldcv(stats + r * W + 1 + e);
+          ps += __ldcv(stats + r * W + 1 + E + e);
+        }
+        a += (cnt / (T * top_k)) * (ps / T);
+      }
+    }
+    *aux = float(double(lbw) * E * a);
+  }
+  __syncthreads();
+  ep_plan_block(s_cnt, s_kept, G, E, rank, s_cap, plan);
+}
+
+// This rank's outputs flag (slot `rank` of the second half) on every rank.
+__global__ void ep_signal_kernel(const uint64_t* __restrict__ peer_flags, int G, int rank,
+                                 int epoch) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  for (int q = 0; q < G; ++q)
+    st_release_sys(reinterpret_cast<int32_t*>(peer_flags[q]) + G + rank, epoch);
 }
 
 // Peer read of a 16-byte vector (plain global load: the data is stable while
@@ -197,7 +321,16 @@ __global__ void __launch_bounds__(256)
     ep_combine_kernel(const uint64_t* __restrict__ peer_y, const int32_t* __restrict__ plan,
                       const int32_t* __restrict__ expert_ids, const float* __restrict__ gate_w,
                       const int32_t* __restrict__ slot_pos, int T, int k, int G, int E, int d8,
-                      int rows_max, uint4* __restrict__ out, int32_t* err) {
+                      int rows_max, uint4* __restrict__ out, int32_t* err,
+                      const int32_t* __restrict__ ready, int epoch) {
+  if (ready) {
+    // every owner's outputs of this step are written (and every owner's gather
+    // of this step has read this rank's tokens)
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) s_ok = wait_flags(ready, G, epoch, err) ? 1 : 0;
+    __syncthreads();
+    if (!s_ok) return;
+  }
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
   const int lane = threadIdx.x & 31;
@@ -324,18 +457,58 @@ extern "C" int lr_ep_gather(const uint64_t* peer_x, const uint64_t* peer_src, co
   return LR_OK;
 }
 
+extern "C" int lr_ep_publish(const uint64_t* peer_stats, const uint64_t* peer_flags,
+                             const int32_t* offsets, const double* prob_sums, int num_tokens,
+                             int world, int num_experts, int rank, int epoch, lr_stream_t stream) {
+  if (!peer_stats || !peer_flags || world < 1 || num_experts < 1 || rank < 0 || rank >= world ||
+      num_tokens < 0 || epoch < 1 || (num_tokens > 0 && (!offsets || !prob_sums)))
+    return LR_ERR_INVALID_ARGUMENT;
+  ep_publish_kernel<<<1, 256, 0, stream>>>(peer_stats, peer_flags, offsets, prob_sums, num_tokens,
+                                           world, num_experts, rank, epoch);
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
+extern "C" int lr_ep_plan_wait(const double* stats, const int32_t* flags, int world,
+                               int num_experts, int rank, int top_k, double capacity_factor,
+                               int max_capacity, float load_balance_weight, int epoch,
+                               int32_t* plan, float* aux_loss, int32_t* err, lr_stream_t stream) {
+  if (!stats || !flags || !plan || !aux_loss || world < 1 || num_experts < 1 ||
+      num_experts % world || rank < 0 || rank >= world || top_k < 1 ||
+      !(capacity_factor > 0) || max_capacity < 1 || epoch < 1 ||
+      world * num_experts > kEpMaxCounts)
+    return LR_ERR_INVALID_ARGUMENT;
+  ep_plan_wait_kernel<<<1, 256, 0, stream>>>(stats, flags, world, num_experts, rank, top_k,
+                                             capacity_factor, max_capacity, load_balance_weight,
+                                             epoch, plan, aux_loss, err);
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
+extern "C" int lr_ep_signal(const uint64_t* peer_flags, int world, int rank, int epoch,
+                            lr_stream_t stream) {
+  if (!peer_flags || world < 1 || rank < 0 || rank >= world || epoch < 1)
+    return LR_ERR_INVALID_ARGUMENT;
+  ep_signal_kernel<<<1, 32, 0, stream>>>(peer_flags, world, rank, epoch);
+  LR_LAUNCH_CHECK();
+  return LR_OK;
+}
+
 extern "C" int lr_ep_combine(const uint64_t* peer_y, const int32_t* plan,
                              const int32_t* expert_ids, const float* gate_weights,
                              const int32_t* slot_pos, int T, int k, int world, int num_experts,
-                             int d, int rows_max, void* out, int32_t* err, lr_stream_t stream) {
+                             int d, int rows_max, void* out, const int32_t* ready_flags,
+                             int epoch, int32_t* err, lr_stream_t stream) {
   if (!peer_y || !plan || !expert_ids || !gate_weights || !slot_pos || !out || T < 0 || k < 1 ||
       k > kMaxTopK || world < 1 || num_experts % world || d <= 0 || d % 8 ||
       (reinterpret_cast<uintptr_t>(out) & 15u))
     return LR_ERR_INVALID_ARGUMENT;
   if (T == 0) return LR_OK;
+  if (ready_flags && epoch < 1) return LR_ERR_INVALID_ARGUMENT;
   ep_combine_kernel<<<(T + 7) / 8, 256, 0, stream>>>(peer_y, plan, expert_ids, gate_weights,
                                                      slot_pos, T, k, world, num_experts, d / 8,
-                                                     rows_max, static_cast<uint4*>(out), err);
+                                                     rows_max, static_cast<uint4*>(out), err,
+                                                     ready_flags, epoch);
   LR_LAUNCH_CHECK();
   return LR_OK;
 }

@@ -465,10 +465,73 @@ at::Tensor ep_gather(const at::Tensor& peer_tokens, const at::Tensor& peer_sourc
   return out;
 }
 
+void ep_publish(const at::Tensor& peer_stats, const at::Tensor& peer_flags,
+                const c10::optional<at::Tensor>& offsets,
+                const c10::optional<at::Tensor>& prob_sums, int64_t num_tokens,
+                int64_t num_experts, int64_t rank, int64_t epoch) {
+  check_cuda(peer_stats, "peer_stats");
+  TORCH_CHECK(peer_stats.scalar_type() == at::kLong && peer_flags.scalar_type() == at::kLong,
+              "peer address arrays: int64");
+  c10::cuda::CUDAGuard g(peer_stats.device());
+  const int32_t* offs = nullptr;
+  const double* ps = nullptr;
+  if (num_tokens > 0) {
+    TORCH_CHECK(offsets.has_value() && prob_sums.has_value(), "offsets / prob_sums needed");
+    TORCH_CHECK(offsets->scalar_type() == at::kInt && offsets->numel() == num_experts + 1,
+                "offsets: (E+1,) int32");
+    TORCH_CHECK(prob_sums->scalar_type() == at::kDouble && prob_sums->numel() == num_experts,
+                "prob_sums: (E,) float64");
+    offs = offsets->data_ptr<int32_t>();
+    ps = prob_sums->data_ptr<double>();
+  }
+  check_status(lr_ep_publish(reinterpret_cast<const uint64_t*>(peer_stats.data_ptr()),
+                             reinterpret_cast<const uint64_t*>(peer_flags.data_ptr()), offs, ps,
+                             int(num_tokens), int(peer_stats.numel()), int(num_experts),
+                             int(rank), int(epoch), cur_stream()),
+               "ep_publish");
+}
+
+std::vector<at::Tensor> ep_plan_wait(const at::Tensor& stats, const at::Tensor& flags,
+                                     int64_t num_experts, int64_t rank, int64_t top_k,
+                                     double capacity_factor, int64_t max_capacity,
+                                     double load_balance_weight, int64_t epoch,
+                                     const c10::optional<at::Tensor>& err) {
+  check_cuda(stats, "stats");
+  check_cuda(flags, "flags");
+  TORCH_CHECK(stats.scalar_type() == at::kDouble && stats.dim() == 2 &&
+                  stats.size(1) == 1 + 2 * num_experts && stats.is_contiguous(),
+              "stats: contiguous (G, 1 + 2E) float64");
+  TORCH_CHECK(flags.scalar_type() == at::kInt && flags.numel() >= 2 * stats.size(0),
+              "flags: (2G,) int32");
+  c10::cuda::CUDAGuard g(stats.device());
+  const int G = int(stats.size(0));
+  const int n = lr_ep_plan_size(G, int(num_experts));
+  TORCH_CHECK(n > 0, "ep_plan_wait: E must be a multiple of G");
+  auto plan = at::empty({n}, stats.options().dtype(at::kInt));
+  auto aux = at::empty({}, stats.options().dtype(at::kFloat));
+  check_status(lr_ep_plan_wait(stats.data_ptr<double>(), flags.data_ptr<int32_t>(), G,
+                               int(num_experts), int(rank), int(top_k), capacity_factor,
+                               int(max_capacity), float(load_balance_weight), int(epoch),
+                               plan.data_ptr<int32_t>(), aux.data_ptr<float>(), err_ptr(err),
+                               cur_stream()),
+               "ep_plan_wait");
+  return {plan, aux};
+}
+
+void ep_signal(const at::Tensor& peer_flags, int64_t rank, int64_t epoch) {
+  check_cuda(peer_flags, "peer_flags");
+  TORCH_CHECK(peer_flags.scalar_type() == at::kLong, "peer address array: int64");
+  c10::cuda::CUDAGuard g(peer_flags.device());
+  check_status(lr_ep_signal(reinterpret_cast<const uint64_t*>(peer_flags.data_ptr()),
+                            int(peer_flags.numel()), int(rank), int(epoch), cur_stream()),
+               "ep_signal");
+}
+
 at::Tensor ep_combine(const at::Tensor& peer_outputs, const at::Tensor& plan,
                       const at::Tensor& expert_ids, const at::Tensor& gate_weights,
                       const at::Tensor& slot_pos, int64_t num_tokens, int64_t num_experts,
-                      int64_t rows_max, int64_t d, const c10::optional<at::Tensor>& err) {
+                      int64_t rows_max, int64_t d, const c10::optional<at::Tensor>& err,
+                      const c10::optional<at::Tensor>& ready_flags, int64_t epoch) {
   check_cuda(plan, "plan");
   TORCH_CHECK(peer_outputs.scalar_type() == at::kLong, "peer address array: int64");
   const int64_t S = expert_ids.numel();
@@ -480,7 +543,11 @@ at::Tensor ep_combine(const at::Tensor& peer_outputs, const at::Tensor& plan,
                              plan.data_ptr<int32_t>(), expert_ids.data_ptr<int32_t>(),
                              gate_weights.data_ptr<float>(), slot_pos.data_ptr<int32_t>(),
                              int(num_tokens), k, int(peer_outputs.numel()), int(num_experts),
-                             int(d), int(rows_max), out.data_ptr(), err_ptr(err), cur_stream()),
+                             int(d), int(rows_max), out.data_ptr(),
+                             ready_flags.has_value() && ready_flags->defined()
+                                 ? ready_flags->data_ptr<int32_t>()
+                                 : nullptr,
+                             int(epoch), err_ptr(err), cur_stream()),
                "ep_combine");
   return out;
 }
@@ -528,8 +595,15 @@ TORCH_LIBRARY(lightning_router, m) {
       "int rank, int max_tokens, int max_slots, int d, Tensor(a!) out, Tensor? err) -> Tensor");
   m.def(
       "ep_combine(Tensor peer_outputs, Tensor plan, Tensor expert_ids, Tensor gate_weights, "
-      "Tensor slot_pos, int num_tokens, int num_experts, int rows_max, int d, Tensor? err) -> "
-      "Tensor");
+      "Tensor slot_pos, int num_tokens, int num_experts, int rows_max, int d, Tensor? err, "
+      "Tensor? ready_flags=None, int epoch=0) -> Tensor");
+  m.def(
+      "ep_publish(Tensor peer_stats, Tensor peer_flags, Tensor? offsets, Tensor? prob_sums, "
+      "int num_tokens, int num_experts, int rank, int epoch) -> ()");
+  m.def(
+      "ep_plan_wait(Tensor stats, Tensor flags, int num_experts, int rank, int top_k, float cf, "
+      "int max_capacity, float lbw, int epoch, Tensor? err) -> Tensor[]");
+  m.def("ep_signal(Tensor peer_flags, int rank, int epoch) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
@@ -547,6 +621,9 @@ TORCH_LIBRARY_IMPL(lightning_router, CUDA, m) {
   m.impl("ep_plan_tokens", &ep_plan_tokens);
   m.impl("ep_gather", &ep_gather);
   m.impl("ep_combine", &ep_combine);
+  m.impl("ep_publish", &ep_publish);
+  m.impl("ep_plan_wait", &ep_plan_wait);
+  m.impl("ep_signal", &ep_signal);
 }
 
 TORCH_LIBRARY_IMPL(lightning_router, CompositeExplicitAutograd, m) {

@@ -30,7 +30,8 @@ C_ABI_SYMBOLS = (
     "lr_combine", "lr_gather_workspace_bytes", "lr_expert_routing_gather",
     "lr_weight_table_bytes", "lr_encode_weight_table",
     "lr_grouped_gemm_workspace_bytes", "lr_grouped_w4a16_gemm", "lr_quantized_matmul",
-    "lr_ep_plan_size", "lr_ep_plan", "lr_ep_plan_tokens", "lr_ep_gather", "lr_ep_combine",
+    "lr_ep_plan_size", "lr_ep_plan", "lr_ep_plan_tokens", "lr_ep_publish", "lr_ep_plan_wait",
+    "lr_ep_signal", "lr_ep_gather", "lr_ep_combine",
     "lr_ipc_export", "lr_ipc_import", "lr_ipc_close",
 )
 
@@ -91,6 +92,7 @@ DEVERR_BITS = {
     0x2: "source token outside [0, T)",
     0x4: "GEMM pipeline wait timed out",
     0x8: "GEMM row segment outside the row range",
+    0x10: "another rank's expert-parallel exchange flag did not arrive in time",
 }
 
 

@@ -27,16 +27,20 @@ output equals the single-GPU output bit for bit.
 Two exchanges implement the moves:
 
 * ``exchange="peer"`` (default with one process per GPU on one node): every rank
-  keeps its tokens, the row -> token map of its expert segments and its expert
-  outputs in buffers the other ranks map through CUDA IPC.  The plan is made on
-  the device from the all-gathered shard sizes and counts (``lr_ep_plan_tokens``:
-  the capacity too), the expert owner pulls its kept rows over NVLink
-  (``lr_ep_gather``) and the token owner pulls the output rows back while it
-  combines them (``lr_ep_combine``).  No host synchronisation; the counts
-  all-gather and one 4-byte all-reduce after the expert GEMMs order the peer
-  reads.  The buffers are sized once for a per-rank shard limit, so shard sizes
-  may differ between ranks and change from step to step (each rank up to the
-  limit) while every rank issues the same collectives in every forward.
+  keeps its tokens, the row -> token map of its expert segments, its expert
+  outputs, a statistics table and a few flags in buffers the other ranks map
+  through CUDA IPC.  A step calls no collective library: each rank writes its
+  statistics row into every rank's table and raises a flag there
+  (``lr_ep_publish``); the plan kernel waits for every rank's flag and decides
+  the capacity and the row layouts on the device (``lr_ep_plan_wait``); the
+  expert owner pulls its kept rows over NVLink (``lr_ep_gather``), runs its
+  GEMMs and raises an "outputs" flag on every rank (``lr_ep_signal``); the token
+  owner waits for those flags and pulls the output rows back while it combines
+  them (``lr_ep_combine``).  Flags carry the step number; every wait is bounded
+  in time and reports through the device error word.  No host synchronisation.
+  The buffers are sized once for a per-rank shard limit, so shard sizes may
+  differ between ranks and change from step to step (each rank up to the
+  limit).
 * ``exchange="nccl"``: kept rows are permuted into a compact send buffer grouped
   by owner rank, exchanged with ``all_to_all_single`` and sent back the same
   way.  The split sizes need one device->host read of the gathered counts per
@@ -156,43 +160,60 @@ class _PeerBuffers:
 
     ``x`` (T_max, d) tokens and ``src`` (T_max*k) row -> token map are read by the
     expert owners; ``y`` (rows_max, d) expert outputs are read by the token owners;
-    ``a`` (rows_max, d) is this rank's GEMM input (local).  ``p*`` hold the G
-    ranks' addresses of each mapped buffer (int64, on the device).
+    ``stats`` (G, 1 + 2E) float64 and ``flags`` (2G,) int32 are written by every
+    rank; ``a`` (rows_max, d) is this rank's GEMM input (local).  ``p*`` hold the
+    G ranks' addresses of each mapped buffer (int64, on the device).
     """
 
     def __init__(self, group, world: int, rank: int, dev, T_max: int, k: int, d: int,
-                 rows_max: int):
+                 rows_max: int, num_experts: int):
         self.T_max, self.rows_max = T_max, rows_max
-        self.x = torch.empty(T_max, d, dtype=torch.float16, device=dev)
-        self.src = torch.zeros(T_max * k, dtype=torch.int32, device=dev)
-        self.y = torch.empty(max(rows_max, 1), d, dtype=torch.float16, device=dev)
+        # one allocation holds every mapped buffer, so each rank exports (and every
+        # peer opens) exactly one IPC handle
+        parts = [("x", torch.float16, (T_max, d)), ("src", torch.int32, (T_max * k,)),
+                 ("y", torch.float16, (max(rows_max, 1), d)),
+                 ("stats", torch.float64, (world, 1 + 2 * num_experts)),
+                 ("flags", torch.int32, (2 * world,))]
+        offs, total = [], 0
+        for _name, dt, shape in parts:
+            n = int(np.prod(shape)) * torch.empty(0, dtype=dt).element_size()
+            offs.append(total)
+            total += (n + 255) // 256 * 256
+        self._mem = torch.empty(total, dtype=torch.uint8, device=dev)
+        views = []
+        for (_name, dt, shape), off in zip(parts, offs):
+            n = int(np.prod(shape)) * torch.empty(0, dtype=dt).element_size()
+            views.append(self._mem.narrow(0, off, n).view(dt).view(shape))
+        self.x, self.src, self.y, self.stats, self.flags = views
+        self.src.zero_()
+        self.stats.zero_()
+        self.flags.zero_()
         self.a = torch.empty(max(rows_max, 1), d, dtype=torch.float16, device=dev)
-        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        # zeroed before any peer can map (and write) them
+        torch.cuda.synchronize(dev)
         lib = _ext.clib()
-        mine = []
-        for t in (self.x, self.src, self.y):
-            h = ctypes.create_string_buffer(64)
-            off = ctypes.c_uint64(0)
-            _check(lib.lr_ipc_export(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)),
-                   "lr_ipc_export")
-            mine.append((h.raw, int(off.value)))
+        h = ctypes.create_string_buffer(64)
+        base_off = ctypes.c_uint64(0)
+        _check(lib.lr_ipc_export(ctypes.c_void_p(self._mem.data_ptr()), h, ctypes.byref(base_off)),
+               "lr_ipc_export")
         allh = [None] * world
-        dist.all_gather_object(allh, mine, group=group)
+        dist.all_gather_object(allh, (h.raw, int(base_off.value)), group=group)
         self._bases = []
-        ptrs = [[0] * world for _ in range(3)]
+        ptrs = [[0] * world for _ in parts]
         for r in range(world):
-            for b, t in enumerate((self.x, self.src, self.y)):
-                if r == rank:
-                    ptrs[b][r] = t.data_ptr()
-                    continue
-                hb, off = allh[r][b]
-                p, base = ctypes.c_void_p(), ctypes.c_void_p()
+            if r == rank:
+                base = self._mem.data_ptr()
+            else:
+                hb, off = allh[r]
+                p, mb = ctypes.c_void_p(), ctypes.c_void_p()
                 _check(lib.lr_ipc_import(ctypes.create_string_buffer(hb, 64), ctypes.c_uint64(off),
-                                         ctypes.byref(p), ctypes.byref(base)), "lr_ipc_import")
-                self._bases.append(base.value)
-                ptrs[b][r] = p.value
-        self.px, self.psrc, self.py = (torch.tensor(p, dtype=torch.int64, device=dev)
-                                       for p in ptrs)
+                                         ctypes.byref(p), ctypes.byref(mb)), "lr_ipc_import")
+                self._bases.append(mb.value)
+                base = p.value
+            for b, off in enumerate(offs):
+                ptrs[b][r] = base + off
+        self.px, self.psrc, self.py, self.pstats, self.pflags = (
+            torch.tensor(p, dtype=torch.int64, device=dev) for p in ptrs)
 
     def close(self) -> None:
         lib = _ext.clib()
@@ -249,6 +270,7 @@ class ExpertParallelMoE:
         self._last_kept_e: list = []
         self._pinned: torch.Tensor | None = None  # reused host staging for per-step metadata
         self.max_tokens_per_rank = max_tokens_per_rank
+        self._epoch = 0  # steps of the peer exchange (the same on every rank)
         self._peer: _PeerBuffers | None = None
         self._plan: torch.Tensor | None = None
 
@@ -275,8 +297,11 @@ class ExpertParallelMoE:
         return cls(layer, world, rank, group, microbatches, exchange, max_tokens_per_rank)
 
     def close(self) -> None:
-        """Unmap the peers' exchange buffers (call before destroying the group)."""
+        """Unmap the peers' exchange buffers (every rank calls it, before destroying
+        the group): a barrier first, so that no rank frees buffers a peer still reads."""
         if self._peer is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
             self._peer.close()
             self._peer = None
 
@@ -307,7 +332,7 @@ class ExpertParallelMoE:
             T_max = max(int(T_max), 1)
             C_max = expert_capacity(T_max * self.world * self.k, self.E, self.cf)
             self._peer = _PeerBuffers(self.group, self.world, self.rank, dev, T_max, self.k, d,
-                                      self.El * C_max)
+                                      self.El * C_max, self.E)
             self._peer_C = C_max
         if T_l > self._peer.T_max:
             raise ValueError(f"shard of {T_l} tokens exceeds the expert-parallel limit of "
@@ -326,10 +351,13 @@ class ExpertParallelMoE:
         dev = x.device
         x = x.to(torch.float16).contiguous()
         T_l, d = x.shape
-        E, G, El, k = self.E, self.world, self.El, self.k
+        E, El, k = self.E, self.El, self.k
         C_max = self._peer_C
         err = _ext.error_word(dev.index)
+        self._epoch += 1
+        epoch = self._epoch
         self._mark("begin")
+        offs = psum = None
         if T_l:
             logits = self.layer.gate.logits(x)
             self._mark("gate")
@@ -338,39 +366,27 @@ class ExpertParallelMoE:
             # this rank's tokens and its uncapped row -> token map, readable by the owners
             bufs.x[:T_l].copy_(x)
             ops.route_rows(ids, gw, offs, pos, ws, T_l, E, bufs.src)
-            cnt = (offs[1:] - offs[:-1]).double()
-        else:  # an empty shard still takes part in every collective and owns its experts
+        else:  # an empty shard still publishes (zeros) and owns its experts
             self._mark("gate")
-            cnt = torch.zeros(E, dtype=torch.float64, device=dev)
-            psum = torch.zeros(E, dtype=torch.float64, device=dev)
-        stats_l = torch.cat([torch.full((1,), float(T_l), dtype=torch.float64, device=dev),
-                             cnt, psum])
-        stats = torch.empty(G * stats_l.numel(), dtype=torch.float64, device=dev)
-        # after the writes above on every rank: the gather below may read them
-        dist.all_gather_into_tensor(stats, stats_l, group=self.group)
-        st = stats.view(G, -1)
-        counts = st[:, 1:1 + E].round().to(torch.int32).contiguous()
-        shard_tokens = st[:, 0].round().to(torch.int32).contiguous()
-        # capacity from the global slot count, decided on the device
-        plan = ops.ep_plan_tokens(counts, shard_tokens, self.rank, k, float(self.cf), C_max, err)
+        # statistics to every rank, then the plan once every rank's row is in
+        ops.ep_publish(bufs.pstats, bufs.pflags, offs, psum, T_l, E, self.rank, epoch)
+        plan, aux = ops.ep_plan_wait(bufs.stats, bufs.flags, E, self.rank, k, float(self.cf),
+                                     C_max, float(self.lbw), epoch, err)
         a = ops.ep_gather(bufs.px, bufs.psrc, plan, E, self.rank, bufs.T_max, bufs.T_max * k,
                           d, bufs.a, err)
         self._mark("dispatch")
         self.layer.experts.forward_segments(a, plan[0:El], plan[El:2 * El], C_max,
                                             first_expert=self.rank * El, num_local=El,
                                             mark=self._mark, out=bufs.y)
-        # every owner's outputs are written before any rank reads them
-        dist.all_reduce(bufs.flag, group=self.group)
+        # this rank's outputs are written: raise its flag on every rank
+        ops.ep_signal(bufs.pflags, self.rank, epoch)
         self._mark("a2a_combine")
         if T_l:
-            out = ops.ep_combine(bufs.py, plan, ids, gw, pos, T_l, E, bufs.rows_max, d, err)
+            out = ops.ep_combine(bufs.py, plan, ids, gw, pos, T_l, E, bufs.rows_max, d, err,
+                                 bufs.flags[self.world:], epoch)
         else:
             out = torch.empty(0, d, dtype=torch.float16, device=dev)
         self._mark("combine")
-        T_all = st[:, 0].sum()
-        f = counts.sum(0).double() / torch.clamp(T_all * k, min=1.0)
-        P = st[:, 1 + E:].sum(0) / torch.clamp(T_all, min=1.0)
-        aux = (self.lbw * E * (f * P).sum()).float()
         self._plan = plan
         return out, aux
 

@@ -30,7 +30,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, wname, overrides, exchange, q):
+def _worker(rank, world, port, wname, overrides, exchange, q, shards=None):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -42,13 +42,20 @@ def _worker(rank, world, port, wname, overrides, exchange, q):
         from lightning_router.workloads import WORKLOADS, build_layer
         w = dataclasses.replace(WORKLOADS[wname], **overrides)
         layer, t = build_layer(w, device=dev)
-        Tl = w.tokens // world
+        if shards is None:
+            shards = [w.tokens // world] * world
+        lo = sum(shards[:rank])
+        x_l = t.x[lo:lo + shards[rank]]
         ep = ExpertParallelMoE.from_layer(layer, world, rank, exchange=exchange)
-        out, aux = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
-        out2, _ = ep.forward(t.x[rank * Tl:(rank + 1) * Tl])
+        out, aux = ep.forward(x_l)
+        out2, _ = ep.forward(x_l)
         same = bool(torch.equal(out, out2))
-        gathered = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(gathered, out)
+        # equal-size gather (shards may differ): pad to the largest shard
+        pad = torch.zeros(max(shards), w.d_model, dtype=out.dtype, device=dev)
+        pad[:out.shape[0]].copy_(out)
+        padded = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(padded, pad)
+        gathered = [p[:n] for p, n in zip(padded, shards)]
         if rank == 0:
             ref, ref_aux = layer(t.x)
             full = torch.cat(gathered)
@@ -74,6 +81,36 @@ def test_expert_parallel_matches_single_gpu(world, wname, overrides, exchange):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, wname, overrides, exchange, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert res[0] == "ok", res[1]
+    _, equal, maxdiff, aux, ref_aux, repeat_same = res
+    assert repeat_same
+    assert equal, f"EP output differs from single GPU (max |diff| {maxdiff})"
+    assert abs(aux - ref_aux) <= 1e-6 * abs(ref_aux)
+
+
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("shards", [[1200, 848], [700, 0, 900, 448]])
+def test_expert_parallel_unequal_shards(shards, exchange):
+    """Ranks with different (and empty) token shards: the peer exchange decides the
+    capacity on the device from the gathered sizes, the NCCL exchange plans on the
+    host; both match the single-GPU layer on the whole batch bit for bit (the shard
+    limit keeps the GEMM's tile class, so the per-row arithmetic is the same)."""
+    world = len(shards)
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    over = dict(tokens=sum(shards), d_model=1024, d_ff=2048)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, "prefill", over, exchange, q, shards))
              for r in range(world)]
     for p in procs:
         p.start()
