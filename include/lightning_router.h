@@ -135,8 +135,9 @@ int lr_permute_tokens(const void* x, int T, int d, int E, int k, int capacity,
  * 256) must fit in 1 MiB: about 2 M tokens at E = 8, about 260 K tokens at
  * E = 64.  Larger sizes return LR_ERR_TOO_LARGE before any work is queued.
  * The first call on a device looks the array's device address up
- * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture begins.  Every call uses the same array and clears the
+ * (cudaGetSymbolAddress) with that device current, and so does the first call
+ * after the device's context changed (a cudaDeviceReset); make such a call
+ * before any stream capture begins.  Every call uses the same array and clears the
  * part that must start at zero, so calls that overlap on the GPU (other
  * streams, other host threads) race and must be serialised by the caller.
  * It allocates and frees nothing.                                          */

@@ -1262,29 +1262,58 @@ extern "C" int lr_expert_routing_gather(const void* y, const float* routing_w,
 // cudaMalloc (it synchronises the whole device).  For them the route scratch
 // lives in this file-scope device array instead of a caller workspace.  Every
 // GPU that loads the library holds it until the process exits.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 static constexpr size_t kStaticRouteScratchBytes = size_t(1) << 20;  // 1 MiB
 static __device__ __align__(256) unsigned char g_route_scratch[kStaticRouteScratchBytes];
 
 static std::mutex g_route_scratch_mu;
-static void* g_route_scratch_dev[64];  // device address per device ordinal, found once
+// Device address per device ordinal, with the context it was found in.
+struct RouteScratchAddr {
+  CUcontext ctx;
+  void* ptr;
+};
+static RouteScratchAddr g_route_scratch_dev[64];
+
+static PFN_cuCtxGetCurrent_v4000 get_ctx_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }
+  return fn;
+}
 
 // Device address of g_route_scratch on the current device.  In host code the
 // array's name is only a host-side stand-in, so the address is looked up with
-// cudaGetSymbolAddress the first time each device calls, with that device current.
+// cudaGetSymbolAddress, with that device current, the first time the device's
+// current context calls; a new context (after cudaDeviceReset, for one) looks
+// it up again.  Ordinals of 64 and above are looked up on every call.
 static int route_scratch_address(void** out) {
   int dev = 0;
   LR_CUDA_TRY(cudaGetDevice(&dev));
+  auto ctx_fn = get_ctx_fn();
+  // null until the runtime has made a context current on this thread
+  auto current_ctx = [&]() -> CUcontext {
+    CUcontext c = nullptr;
+    if (!ctx_fn || ctx_fn(&c) != CUDA_SUCCESS) c = nullptr;
+    return c;
+  };
+  CUcontext ctx = current_ctx();
   std::lock_guard<std::mutex> lock(g_route_scratch_mu);
-  if (dev < 64 && g_route_scratch_dev[dev]) {
-    *out = g_route_scratch_dev[dev];
+  if (dev < 64 && ctx && g_route_scratch_dev[dev].ptr && g_route_scratch_dev[dev].ctx == ctx) {
+    *out = g_route_scratch_dev[dev].ptr;
     return LR_OK;
   }
   void* p = nullptr;
   const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
   if (e != cudaSuccess || p == nullptr) return record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-  if (dev < 64) g_route_scratch_dev[dev] = p;
+  if (dev < 64) g_route_scratch_dev[dev] = {current_ctx(), p};
   *out = p;
   return LR_OK;
 }

@@ -1,8 +1,8 @@
 """Generate golden vectors from the reference implementation itself.
 
-Run in the build container, where the reference checkout is mounted read-only:
+Run where a checkout of the reference is available (read-only is enough):
 
-    LR_REFERENCE_PATH=/root/reference python tests/golden/make_golden.py
+    LR_REFERENCE_PATH=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference package ``lightning_router`` from that checkout and
 runs, on seeded inputs:
@@ -31,7 +31,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np
 import torch
 
-REF = os.environ.get("LR_REFERENCE_PATH", "/root/reference")
+REF = os.environ.get("LR_REFERENCE_PATH")
+if not REF:
+    raise SystemExit("set LR_REFERENCE_PATH to a checkout of the reference repository")
 OUT = Path(__file__).resolve().parent
 
 
