@@ -155,6 +155,55 @@ inline int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
   return r == CUDA_SUCCESS ? LR_OK : LR_ERR_INVALID_ARGUMENT;
 }
 
+// SM count of the current device (queried once per device ordinal below 64).
+inline int current_sm_count(int* out) {
+  static int cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return LR_ERR_NO_DEVICE;
+  if (dev < 64 && __atomic_load_n(&cache[dev], __ATOMIC_RELAXED) > 0) {
+    *out = cache[dev];
+    return LR_OK;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return LR_ERR_NO_DEVICE;
+  if (dev < 64) __atomic_store_n(&cache[dev], sms, __ATOMIC_RELAXED);
+  *out = sms;
+  return LR_OK;
+}
+
+// Tensor map of a row-major fp16 operand (K columns, R rows, box of 64 x
+// box_rows), reused while the same host thread passes the same operand: a
+// small per-thread cache keyed by device, address, shape, box and swizzle.
+inline int encode_rows_cached(CUtensorMap* out, const void* A, int K, int R, uint32_t box_rows,
+                              CUtensorMapSwizzle sw) {
+  struct Entry {
+    const void* a;
+    int K, R, dev;
+    uint32_t box;
+    int sw;
+    CUtensorMap map;
+  };
+  thread_local Entry cache[8];
+  thread_local int used = 0, next = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return LR_ERR_NO_DEVICE;
+  for (int i = 0; i < used; ++i) {
+    const Entry& c = cache[i];
+    if (c.a == A && c.K == K && c.R == R && c.dev == dev && c.box == box_rows && c.sw == int(sw)) {
+      *out = c.map;
+      return LR_OK;
+    }
+  }
+  const int rc = encode_2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
+                           uint64_t(K) * 2, kBK, box_rows, sw);
+  if (rc) return rc;
+  cache[next] = Entry{A, K, R, dev, box_rows, int(sw), *out};
+  next = (next + 1) % 8;
+  if (used < 8) ++used;
+  return LR_OK;
+}
+
 // Grouped GEMM for expert segments of at most kSkinnyMaxRows rows (decode):
 // mma.sync with the weights as the M operand (lr_w4a16_skinny.cu).  Needs
 // K % 8 == 0 (16-byte token rows for TMA) and a group size that is a power of

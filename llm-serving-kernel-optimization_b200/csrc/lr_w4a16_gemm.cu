@@ -530,12 +530,11 @@ static int launch_gemm(const void* A, int K, int R, const ExpertEntry* table, in
   static unsigned long long configured = 0;
   if (const int rc = set_dyn_smem_once(kern, S::kTotal, configured)) return rc;
   CUtensorMap ta;
-  const int rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
-                           uint64_t(K) * 2, kBK, uint32_t(S::ROWS), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  int dev = 0, sms = 0;
-  LR_CUDA_TRY(cudaGetDevice(&dev));
-  LR_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  if (const int rc = encode_rows_cached(&ta, A, K, R, uint32_t(S::ROWS),
+                                        CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  int sms = 0;
+  if (const int rc = current_sm_count(&sms)) return rc;
   constexpr int BO = (MODE == LR_FFN_MODE_SWIGLU) ? S::WN / 2 : S::WN;
   const long n_tiles = (N + BO - 1) / BO;
   const long upper = long(E) * ((max_rows + S::ROWS - 1) / S::ROWS) * n_tiles;

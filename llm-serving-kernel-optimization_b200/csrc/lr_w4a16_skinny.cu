@@ -507,9 +507,8 @@ static int launch_skinny_shape(const void* A, int K, int R, const ExpertEntry* t
   static unsigned long long configured = 0;
   if (const int rc = set_dyn_smem_once(kern, S::kTotal, configured, true)) return rc;
   CUtensorMap ta;
-  const int rc = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, uint64_t(K), uint64_t(R),
-                           uint64_t(K) * 2, kBK, uint32_t(S::TR), CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
+  if (const int rc = encode_rows_cached(&ta, A, K, R, uint32_t(S::TR), CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
   constexpr int BO = MODE == LR_FFN_MODE_SWIGLU ? S::NB * 32 : S::NB * 64;
   const int n_slabs = (N + BO - 1) / BO;
   const int m_tiles = (max_rows + S::TR - 1) / S::TR;

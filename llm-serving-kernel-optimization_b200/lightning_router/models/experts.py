@@ -23,6 +23,10 @@ from lightning_router.kernels.quantized_matmul import (
     weight_table)
 
 
+def _first_ptr(objs) -> int:
+    return next((t.data_ptr() for t in objs if t is not None), 0)
+
+
 def _module_table(cache: dict, q, s, z, n, d, f, g, gated) -> WeightTable:
     """Per-module table cache keyed by the buffers' addresses and shapes."""
     key = table_key(q, s, z, n, d, f, g, gated)
@@ -124,21 +128,34 @@ class ExpertGroup(nn.Module):
             for _ in range(num_experts)
         ])
 
+    def _buffer_objects(self, first: int, count: int) -> tuple:
+        # the experts' registered buffers, read from the modules' buffer dicts
+        # (plain dict iteration: this runs on every forward)
+        mods = self.experts._modules
+        return tuple(b for e in range(first, first + count)
+                     for b in mods[str(e)]._buffers.values())
+
     def table(self, first: int = 0, count: int | None = None) -> WeightTable:
         count = self.num_experts - first if count is None else count
+        hit = self._tables.get((first, count))
+        objs = self._buffer_objects(first, count)
+        # The table holds the buffers' addresses.  ``.to()`` / ``.cuda()`` or
+        # reassigning a buffer creates new tensor objects; loading a state dict
+        # copies in place and keeps the addresses.  So the table is reused while
+        # the buffer objects (and the first one's address) are unchanged.
+        if hit is not None and len(hit[0]) == len(objs) and \
+                all(a is b for a, b in zip(hit[0], objs)) and hit[1] == _first_ptr(objs):
+            return hit[2]
         q, s, z = [], [], []
         for e in range(first, first + count):
             qe, se, ze = self.experts[e].quant_tensors()
             q += qe
             s += se
             z += ze
-        key = table_key(q, s, z)
-        hit = self._tables.get((first, count))
-        if hit is None or hit[0] != key:  # first use, or the buffers moved / were replaced
-            wt = weight_table(q, s, z, count, self.hidden_size, self.intermediate_size,
-                              self.group_size, self.activation == "swiglu", cache=False)
-            hit = self._tables[(first, count)] = (key, wt)
-        return hit[1]
+        wt = weight_table(q, s, z, count, self.hidden_size, self.intermediate_size,
+                          self.group_size, self.activation == "swiglu", cache=False)
+        self._tables[(first, count)] = (objs, _first_ptr(objs), wt)
+        return wt
 
     def forward_segments(self, x: torch.Tensor, seg_start: torch.Tensor, seg_len: torch.Tensor,
                          max_rows: int, first_expert: int = 0,
