@@ -124,3 +124,62 @@ def test_expert_parallel_unequal_shards(shards, exchange):
     assert repeat_same
     assert equal, f"EP output differs from single GPU (max |diff| {maxdiff})"
     assert abs(aux - ref_aux) <= 1e-6 * abs(ref_aux)
+
+
+def _worker_ep(rank, world, port, ckpt_dir, q):
+    """One rank of ExpertParallelWorker (the replacement of the reference's
+    TensorParallelGroup, serving/worker.py:81-186) loading a checkpoint through
+    its own interface."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        from lightning_router.serving.worker import ExpertParallelWorker
+        from lightning_router.workloads import WORKLOADS, build_layer
+        w = dataclasses.replace(WORKLOADS["prefill"], tokens=1024, d_model=1024, d_ff=2048)
+        layer, t = build_layer(w, device=dev)
+        path = os.path.join(ckpt_dir, f"moe{rank}.pt")
+        torch.save({k: v.cpu() for k, v in layer.state_dict().items()}, path)
+        cfg = (dict(hidden_size=w.d_model, intermediate_size=w.d_ff),
+               dict(num_experts=w.experts, num_experts_per_token=w.top_k,
+                    expert_capacity_factor=w.capacity_factor, expert_activation=w.activation),
+               dict(group_size=w.group_size), {}, {"ep_exchange": "peer"})
+        wk = ExpertParallelWorker(*cfg, rank=rank, world=world)
+        wk.init_device()
+        wk.load_model(path)
+        Tl = w.tokens // world
+        out = wk.execute_model(None, t.x[rank * Tl:(rank + 1) * Tl].view(1, Tl, -1))
+        gathered = [torch.empty(Tl, w.d_model, dtype=out.dtype, device=dev) for _ in range(world)]
+        dist.all_gather(gathered, out.reshape(Tl, -1).contiguous())
+        if rank == 0:
+            ref, _ = layer(t.x)
+            full = torch.cat(gathered)
+            q.put(("ok", bool(torch.equal(full, ref)),
+                   float((full.float() - ref.float()).abs().max()), None, None, True))
+        wk.shutdown()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("err", traceback.format_exc(), None, None, None, None))
+
+
+def test_expert_parallel_worker_matches_single_gpu(tmp_path):
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_ep, args=(r, world, port, str(tmp_path), q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert res[0] == "ok", res[1]
+    assert res[1], f"ExpertParallelWorker output differs from single GPU (max |diff| {res[2]})"
