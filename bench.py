@@ -166,8 +166,9 @@ def cpu_port_setup(w):
     from lightning_router.workloads import make_layer
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     t = make_layer(w, device=dev, gen_device=dev)
-    experts = [{n: dequantize_tensor(q, s, z, w.group_size, s.shape[1]).float().cpu()
-                for n, (q, s, z) in ex.items()} for ex in t.experts]
+    # nn.Linear layout (out, in), as the reference's unquantized experts hold them
+    experts = [{n: dequantize_tensor(q, s, z, w.group_size, s.shape[1]).float().t().contiguous()
+                .cpu() for n, (q, s, z) in ex.items()} for ex in t.experts]
     x = t.x.float().cpu()
     wg = t.gate_w.float().cpu()
     bias = None if t.bias is None else t.bias.float().cpu()

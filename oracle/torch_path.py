@@ -18,8 +18,9 @@ reference's own outputs in ``tests/golden/layer_torch.npz``):
   capacity is applied on this path;
 * ``ExpertFFN.forward`` unquantized (``lightning_router/models/experts.py:71-89``):
   ``down(silu(gate x) * up x)``, here with the dequantized INT4 weights in fp32
-  (``W`` stored (K = in, N = out), so ``x @ W`` is ``nn.Linear`` with weight
-  ``W.T``).  ``gated=False`` gives the ``down(silu(up x))`` expert of the
+  held as ``nn.Linear`` holds them, (out, in) row-major, and applied with
+  ``F.linear`` (:func:`linear_experts` converts the packed format's (in, out)
+  matrices once).  ``gated=False`` gives the ``down(silu(up x))`` expert of the
   non-gated configuration.
 
 The routing-only sweep baseline restates ``vectorized_pytorch_routing``
@@ -32,7 +33,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-__all__ = ["gate", "expert_ffn", "moe_layer", "vectorized_routing"]
+__all__ = ["gate", "linear_experts", "expert_ffn", "moe_layer", "vectorized_routing"]
 
 
 def gate(x: torch.Tensor, wg: torch.Tensor, k: int, load_balance_weight: float = 0.01,
@@ -57,16 +58,23 @@ def gate(x: torch.Tensor, wg: torch.Tensor, k: int, load_balance_weight: float =
     return ids, w, tok, aux
 
 
+def linear_experts(experts: list) -> list:
+    """(in, out) fp32 matrices (the packed format's K x N) -> ``nn.Linear`` weights
+    (out, in), contiguous, as the reference's unquantized experts store them."""
+    return [{m: W.t().contiguous() for m, W in ex.items()} for ex in experts]
+
+
 def expert_ffn(x: torch.Tensor, w: dict, gated: bool = True) -> torch.Tensor:
-    """experts.py:71-89 with fp32 weights ``w["gate"|"up"|"down"]`` of shape (in, out)."""
+    """experts.py:71-89 with ``nn.Linear`` weights ``w["gate"|"up"|"down"]`` (out, in)."""
     if gated:
-        return (F.silu(x @ w["gate"]) * (x @ w["up"])) @ w["down"]
-    return F.silu(x @ w["up"]) @ w["down"]
+        return F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]), w["down"])
+    return F.linear(F.silu(F.linear(x, w["up"])), w["down"])
 
 
 def moe_layer(x: torch.Tensor, wg: torch.Tensor, experts: list, k: int, gated: bool = True,
               load_balance_weight: float = 0.01, bias: torch.Tensor | None = None):
-    """``(out, aux_loss)`` of the reference's torch-routing layer, moe_layer.py:64-135."""
+    """``(out, aux_loss)`` of the reference's torch-routing layer, moe_layer.py:64-135;
+    ``experts`` in ``nn.Linear`` layout (:func:`linear_experts`)."""
     ids, w, tok, aux = gate(x, wg, k, load_balance_weight, bias)
     out = torch.zeros_like(x)
     for e in range(len(experts)):

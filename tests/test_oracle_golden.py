@@ -129,7 +129,7 @@ def test_torch_path_port_matches_reference_layer(name):
         experts.append(ex)
     x = torch.from_numpy(z[f"{name}_x"]).reshape(-1, d)
     wg = torch.from_numpy(z[f"{name}_wg"])
-    out, aux = torch_path.moe_layer(x, wg, experts, k)
+    out, aux = torch_path.moe_layer(x, wg, torch_path.linear_experts(experts), k)
     ref = z[f"{name}_out"].reshape(-1, d)
     np.testing.assert_allclose(out.numpy(), ref, rtol=1e-5, atol=1e-6)
     assert abs(float(aux) - float(z[f"{name}_aux"])) <= 1e-6 * abs(float(z[f"{name}_aux"]))
