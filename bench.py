@@ -185,13 +185,14 @@ def cpu_port_step(w, x, wg, bias, experts):
                                 bias=bias)
 
 
-def run_cpu(w, steps: int, warmup: int, step_budget_s: float = 10.0):
+def run_cpu(w, steps: int, warmup: int, step_budget_s: float = 25.0):
     """Times the reference's CPU path (its torch-routing MoELayer in fp32, restated in
     ``oracle/torch_path.py``) with every host thread; returns (tokens/s, sample, threads).
 
     Each step runs the first ``sample`` tokens of the workload, ``sample`` sized by an
-    untimed calibration step so that one step takes about ``step_budget_s`` seconds
-    (at most the whole workload).  The torch path applies no capacity, so the work
+    untimed calibration step on 256 tokens so that one step takes at most about
+    ``step_budget_s`` seconds (at most the whole workload; the calibration's small
+    batches run slower per token, so the timed step is usually shorter).  The torch path applies no capacity, so the work
     per token does not depend on the sample size.
     """
     torch.set_num_threads(os.cpu_count() or 1)

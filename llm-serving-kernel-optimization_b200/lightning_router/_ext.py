@@ -83,8 +83,13 @@ def require_cuda(*tensors: torch.Tensor) -> None:
 
 @functools.lru_cache(maxsize=None)
 def error_word(device_index: int) -> torch.Tensor:
-    """Per-device int32 word the kernels OR contract violations into."""
-    return torch.zeros(1, dtype=torch.int32, device=f"cuda:{device_index}")
+    """Per-device int32 word the kernels OR contract violations into.
+
+    Created as a normal tensor even when the first call comes from inside
+    ``torch.inference_mode`` (an inference tensor could not be reset in place
+    outside it later)."""
+    with torch.inference_mode(False):
+        return torch.zeros(1, dtype=torch.int32, device=f"cuda:{device_index}")
 
 
 DEVERR_BITS = {

@@ -39,6 +39,10 @@ class HostPipeline:
         self.copy_stream = torch.cuda.Stream(device=device)
         # buffer b may be overwritten once the compute that read it finished
         self._free = [None] * self.depth
+        # outputs whose device->host copy may still run, with that copy's event:
+        # held (instead of record_stream, whose deferred frees make every later
+        # allocation poll events) until the compute stream has waited for it
+        self._held = [None] * self.depth
 
     def run(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor]) -> None:
         compute = torch.cuda.current_stream(self.device)
@@ -70,11 +74,18 @@ class HostPipeline:
             done = torch.cuda.Event()
             done.record(compute)
             self._free[b] = done
+            if self._held[b] is not None:
+                # the copy of the output `depth` steps ago is ordered before any
+                # later use of its memory on the compute stream
+                compute.wait_event(self._held[b][1])
             with torch.cuda.stream(cs):
                 cs.wait_event(done)
-                out.record_stream(cs)  # keep the output's memory until the copy ran
                 outputs[i].copy_(out, non_blocking=True)
+                copied = torch.cuda.Event()
+                copied.record(cs)
+            self._held[b] = (out, copied)
             if self.depth == 1 and i + 1 < n:
                 load(i + 1)
         cs.synchronize()
         compute.wait_stream(cs)
+        self._held = [None] * self.depth

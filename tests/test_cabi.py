@@ -91,3 +91,19 @@ def test_cpu_tensors_fail_loudly():
     gate = TopKGating(64, 4, 2)
     with pytest.raises(RuntimeError, match="CUDA"):
         gate(torch.randn(3, 64))
+
+
+
+@pytest.mark.gpu
+def test_error_word_created_in_inference_mode_resets_outside():
+    """The cached device error word stays resettable outside inference mode even
+    when the first kernel call that needed it ran inside inference mode."""
+    import torch
+    _ext.error_word.cache_clear()
+    with torch.inference_mode():
+        w = _ext.error_word(0)
+    assert not w.is_inference()
+    w.fill_(0x8)
+    with pytest.raises(RuntimeError, match="segment"):
+        _ext.check_device_errors(0)
+    assert int(w.item()) == 0
