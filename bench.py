@@ -53,13 +53,17 @@ METRIC = "MoE-layer tokens/s"
 UNIT = "tokens/s"
 
 # DRAM bytes (read + write) per launch of the dominant kernel (the gate/up GEMM),
-# from one ncu capture of this bench's own command per workload:
-#   ncu --clock-control none --metrics dram__bytes_read.sum,dram__bytes_write.sum \
-#       -k regex:w4a16 -c 2 python bench.py --workload W --steps 2 --warmup 3 --no-cpu
-# (the first launch of each GEMM); None until captured for the current kernels.
+# averaged over the launches of the timed loop in one ncu capture of this bench's
+# own command:
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum \
+#       --clock-control none --profile-from-start off \
+#       python bench.py [--workload decode] --steps 2 --warmup 3 --no-cpu
+# prefill: 980.4 MB read (algorithmic 757: token rows 268 + weights 489) and 911.4 MB
+# written (940 of intermediate rows, part still in L2 at the end); decode: 489.8 MB
+# read (the weights of the 8 experts), 2.7 MB written.
 NCU_TRAFFIC = {
-    "prefill": None,
-    "decode": None,
+    "prefill": 980.4e6 + 911.4e6,
+    "decode": 489.8e6 + 2.7e6,
 }
 
 

@@ -7,7 +7,9 @@ way).  :class:`HostPipeline` keeps ``depth`` device input buffers and moves the
 copies to their own stream:
 
 * the host->device copy of batch i+1 runs while batch i computes;
-* the device->host copy of batch i's output runs while batch i+1 computes.
+* the device->host copy of batch i's output runs while batch i+1 computes;
+* the two directions have a stream each, so they overlap one another too (a
+  link carries both directions at once; on one stream they would add up).
 
 Every batch's copies still happen (and are waited for at the end of
 :meth:`HostPipeline.run`); only their overlap with compute changes.  The
@@ -36,7 +38,8 @@ class HostPipeline:
         self.device = device
         self.bufs = [torch.empty(like.shape, dtype=like.dtype, device=device)
                      for _ in range(self.depth)]
-        self.copy_stream = torch.cuda.Stream(device=device)
+        self.copy_stream = torch.cuda.Stream(device=device)      # host -> device
+        self.out_stream = torch.cuda.Stream(device=device)       # device -> host
         # buffer b may be overwritten once the compute that read it finished
         self._free = [None] * self.depth
         # outputs whose device->host copy may still run, with that copy's event:
@@ -46,8 +49,9 @@ class HostPipeline:
 
     def run(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor]) -> None:
         compute = torch.cuda.current_stream(self.device)
-        cs = self.copy_stream
+        cs, os_ = self.copy_stream, self.out_stream
         cs.wait_stream(compute)  # nothing of this run starts before the caller's prior work
+        os_.wait_stream(compute)
         loaded = [None] * self.depth
 
         def load(i: int) -> None:
@@ -78,14 +82,16 @@ class HostPipeline:
                 # the copy of the output `depth` steps ago is ordered before any
                 # later use of its memory on the compute stream
                 compute.wait_event(self._held[b][1])
-            with torch.cuda.stream(cs):
-                cs.wait_event(done)
+            with torch.cuda.stream(os_):
+                os_.wait_event(done)
                 outputs[i].copy_(out, non_blocking=True)
                 copied = torch.cuda.Event()
-                copied.record(cs)
+                copied.record(os_)
             self._held[b] = (out, copied)
             if self.depth == 1 and i + 1 < n:
                 load(i + 1)
         cs.synchronize()
+        os_.synchronize()
         compute.wait_stream(cs)
+        compute.wait_stream(os_)
         self._held = [None] * self.depth
