@@ -368,8 +368,10 @@ def run_gpu(args, ws, rank, local):
         return (out.clone(), aux) if graph is not None else (out, aux)
 
     # timed region (device time, max over ranks).  cudaProfilerStart/Stop bracket
-    # it so `ncu --profile-from-start off` lists exactly the timed launches.
-    stage_owner.stage_events = []
+    # it so `ncu --profile-from-start off` lists exactly the timed launches.  No
+    # stage events are recorded in it: the stage times come from a separate eager
+    # pass afterwards.
+    stage_owner.stage_events = None
     clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
                           else local)
     clocks.start()
@@ -390,17 +392,17 @@ def run_gpu(args, ws, rank, local):
     clk = clocks.stop()
     ms_local = start.elapsed_time(end)
     ms = max_over_ranks(ms_local, ws)
-    if graph is not None:
-        eager_fwd(x)  # one untimed eager pass first: the stage pass times warm launches
-        torch.cuda.synchronize()
-        stage_owner.stage_events = []
-        n_stage = min(args.steps, 10)
-        for _ in range(n_stage):
-            eager_fwd(x)
-        torch.cuda.synchronize()
-        st = stage_times(stage_owner.stage_events, n_stage)
-    else:
-        st = stage_times(stage_owner.stage_events, args.steps)
+    # stage times: an extra eager pass (after one untimed forward, so it times
+    # warm launches); every rank runs it, so the exchange's collectives match
+    eager = eager_fwd if graph is not None else fwd
+    eager(x)
+    torch.cuda.synchronize()
+    stage_owner.stage_events = []
+    n_stage = min(args.steps, 10)
+    for _ in range(n_stage):
+        eager(x)
+    torch.cuda.synchronize()
+    st = stage_times(stage_owner.stage_events, n_stage)
     stage_owner.stage_events = None
     value = w.tokens * args.steps / (ms / 1e3)
 
@@ -438,6 +440,13 @@ def run_gpu(args, ws, rank, local):
         launches_per_step = 8 if args.exchange == "peer" else 6
     else:
         launches_per_step = 5 if w.tokens <= SMALL_BATCH_TOKENS else 6
+    # segments of at most 32 rows on 8-bit operands: each GEMM adds its token-term pass
+    from lightning_router.kernels import quantized_matmul as qm
+    from lightning_router.kernels.expert_routing import expert_capacity
+    cap = expert_capacity(T_local * ws * w.top_k, w.experts, w.capacity_factor)
+    if qm.INT8_OPERANDS and cap <= 32 and w.group_size % 128 == 0 and \
+            w.d_model % 128 == 0 and w.d_ff % 128 == 0:
+        launches_per_step += 2
     if ws > 1:
         barrier(ws)
         model.close()
@@ -447,6 +456,7 @@ def run_gpu(args, ws, rank, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": workload_desc(w), "global_batch": w.tokens, "seq_len": None,
                    "parallelism": parallel,
+                   **({"gemm_operands": "f16"} if args.operands == "f16" else {}),
                    **({"exchange": args.exchange} if ws > 1 else {}),
                    **({"cuda_graph": True} if graph is not None else {}),
                    "l2": "inputs larger than L2 (INT4 weights "
@@ -564,7 +574,13 @@ def main():
                     help="one GPU: replay the layer forward as a captured CUDA graph")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel token exchange (N > 1)")
+    ap.add_argument("--operands", default="auto", choices=["auto", "f16"],
+                    help="expert GEMM operands: auto (8-bit for segments of at most 32 "
+                         "rows) or f16 everywhere")
     args = ap.parse_args()
+    if args.operands == "f16":
+        from lightning_router.kernels import quantized_matmul as qm
+        qm.INT8_OPERANDS = False
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = init_dist()

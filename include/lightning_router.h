@@ -206,7 +206,21 @@ size_t lr_weight_table_bytes(int num_experts);
 int lr_encode_weight_table(const lr_expert_weights* experts, int E, int d_model, int d_ff,
                            int group_size, int gated, void* host_table, size_t table_bytes);
 
+/* Workspace of lr_grouped_w4a16_gemm: 0 when the call needs none.  Superseded
+ * by lr_grouped_w4a16_workspace_bytes (ABI 3); kept for ABI 2 callers.        */
 size_t lr_grouped_gemm_workspace_bytes(int num_experts);
+
+/* Workspace (bytes, 128-byte aligned) that lets lr_grouped_w4a16_gemm take its
+ * 8-bit path for this shape: expert segments of at most 32 rows with
+ * K % 128 == 0, group_size % 128 == 0 and N % 32 == 0 (decode).  There the
+ * token rows are written as two signed 8-bit terms per 128-k block
+ * (x ~ sigma * (a1 + a2/256), sigma = max|x|/127 of the block; error at most
+ * sigma/512) and the INT4 codes enter the tensor core as unsigned bytes; the
+ * group scale and zero are applied in fp32 per 128-k block.  Returns 0 for
+ * shapes that do not take that path.  Without the workspace the same call
+ * runs the fp16-operand kernel.                                               */
+size_t lr_grouped_w4a16_workspace_bytes(int num_experts, int R, int K, int N, int group_size,
+                                        int max_rows_per_expert);
 
 /* Grouped W4A16 GEMM.  For each expert e, rows
  * [seg_start[e], seg_start[e] + seg_len[e]) of A (R x K fp16, row-major)
@@ -214,8 +228,10 @@ size_t lr_grouped_gemm_workspace_bytes(int num_experts);
  * written to the same rows of C (R x N_out fp16).  seg_* live on the device.
  * `max_rows_per_expert` bounds seg_len (selects the token tile); seg_len
  * beyond it is clamped and flagged.  `group_size` is the one the table was
- * encoded with.  The kernel follows the shape: tcgen05 (tokens the UMMA M
- * operand) when K % 64 == 0, group_size % 64 == 0 and N % 32 == 0; mma.sync
+ * encoded with.  The kernel follows the shape: tcgen05 on 8-bit operands for
+ * segments of at most 32 rows when the workspace holds
+ * lr_grouped_w4a16_workspace_bytes(...) bytes; tcgen05 on fp16 operands (tokens
+ * the UMMA M operand) when K % 64 == 0, group_size % 64 == 0 and N % 32 == 0; mma.sync
  * with the weights as the M operand when K % 8 == 0, N % 32 == 0 and
  * group_size is a power of two >= 16; otherwise CUDA cores.  A needs 2-byte,
  * C 16-byte alignment.

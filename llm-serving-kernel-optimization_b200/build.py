@@ -28,8 +28,8 @@ OBJ_DIR = HERE / "_build"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 
-CU_SOURCES = ["lr_capi.cu", "lr_routing.cu", "lr_w4a16_gemm.cu", "lr_w4a16_skinny.cu",
-              "lr_w4a16_generic.cu", "lr_ep.cu"]
+CU_SOURCES = ["lr_capi.cu", "lr_routing.cu", "lr_w4a16_gemm.cu", "lr_w4a16_i8.cu",
+              "lr_w4a16_skinny.cu", "lr_w4a16_generic.cu", "lr_ep.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

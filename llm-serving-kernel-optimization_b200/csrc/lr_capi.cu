@@ -12,7 +12,7 @@ int record_cuda_error(cudaError_t e) {
 
 extern "C" int lr_last_cuda_error(void) { return lr::g_last_cuda_error; }
 
-extern "C" int lr_abi_version(void) { return 2; }
+extern "C" int lr_abi_version(void) { return 3; }
 
 extern "C" const char* lr_status_string(int status) {
   switch (status) {

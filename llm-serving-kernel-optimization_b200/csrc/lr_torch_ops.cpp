@@ -349,7 +349,7 @@ at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int6
                               const c10::optional<at::Tensor>& seg_start,
                               const c10::optional<at::Tensor>& seg_len, int64_t max_rows,
                               const c10::optional<at::Tensor>& out,
-                              const c10::optional<at::Tensor>& err) {
+                              const c10::optional<at::Tensor>& err, bool int8_operands) {
   check_cuda(table, "table");
   check_cuda(A, "A");
   TORCH_CHECK(A.dim() == 2 && A.scalar_type() == at::kHalf, "A: (R,K) fp16");
@@ -372,10 +372,18 @@ at::Tensor grouped_w4a16_gemm(const at::Tensor& table, int64_t num_experts, int6
     ss = seg_start->data_ptr<int32_t>();
     sl = seg_len->data_ptr<int32_t>();
   }
+  // the 8-bit path (short segments) writes the token terms into a workspace
+  const size_t wsb = int8_operands
+                         ? lr_grouped_w4a16_workspace_bytes(int(num_experts), int(A.size(0)),
+                                                            int(A.size(1)), int(N),
+                                                            int(group_size), int(max_rows))
+                         : 0;
+  at::Tensor ws;
+  if (wsb) ws = workspace(wsb, A);
   check_status(lr_grouped_w4a16_gemm(table.data_ptr(), int(num_experts), int(mode), int(mat),
                                      A.data_ptr(), int(A.size(0)), int(A.size(1)), int(N),
-                                     int(group_size), ss, sl, int(max_rows), C.data_ptr(), nullptr,
-                                     0, err_ptr(err),
+                                     int(group_size), ss, sl, int(max_rows), C.data_ptr(),
+                                     wsb ? ws.data_ptr() : nullptr, wsb, err_ptr(err),
                                      cur_stream()),
                "grouped_w4a16_gemm");
   return C;
@@ -582,7 +590,7 @@ TORCH_LIBRARY(lightning_router, m) {
   m.def(
       "grouped_w4a16_gemm(Tensor table, int num_experts, int mode, int mat, Tensor A, int N, "
       "int group_size, Tensor? seg_start, Tensor? seg_len, int max_rows, Tensor? out, "
-      "Tensor? err) -> Tensor");
+      "Tensor? err, bool int8_operands=True) -> Tensor");
   m.def(
       "route_rows(Tensor expert_ids, Tensor gate_weights, Tensor row_offsets, Tensor(a!) "
       "slot_pos, Tensor ws, int num_tokens, int num_experts, Tensor(b!) source_idx) -> Tensor");

@@ -215,6 +215,17 @@ template <int MODE>
 int launch_generic(const void* A, int K, int R, const ExpertEntry* table, int E, int mat, int N,
                    int group_size, const int32_t* seg_start, const int32_t* seg_len,
                    int max_rows, __half* C, int32_t* err, cudaStream_t stream);
+// Grouped GEMM for expert segments of at most 32 rows on 8-bit tcgen05 operands
+// (lr_w4a16_i8.cu): INT4 codes as unsigned bytes, token rows as two signed
+// 8-bit terms per 128-k block, group scale and zero folded per block.  Needs
+// K % 128 == 0, group_size % 128 == 0, N % 32 == 0 and a workspace of
+// i8_workspace_bytes(R, K) bytes (128-byte aligned) for the token terms.
+bool i8_eligible(int K, int N, int group_size, int max_rows);
+size_t i8_workspace_bytes(int R, int K);
+template <int MODE>
+int launch_i8(const void* A, int K, int R, const ExpertEntry* table, int E, int mat, int N,
+              int group_size, const int32_t* seg_start, const int32_t* seg_len, int max_rows,
+              __half* C, void* ws, int32_t* err, cudaStream_t stream);
 template <int MODE>
 int launch_skinny(const void* A, int K, int R, const ExpertEntry* table, int E, int mat, int N,
                   const int32_t* seg_start, const int32_t* seg_len, int max_rows, __half* C,

@@ -625,13 +625,18 @@ extern "C" size_t lr_grouped_gemm_workspace_bytes(int num_experts) {
   return 0;
 }
 
+extern "C" size_t lr_grouped_w4a16_workspace_bytes(int num_experts, int R, int K, int N,
+                                                   int group_size, int max_rows_per_expert) {
+  if (num_experts < 1 || R < 1 || K < 1 || group_size < 1 || K % group_size != 0) return 0;
+  if (!i8_eligible(K, N, group_size, max_rows_per_expert)) return 0;
+  return i8_workspace_bytes(R, K);
+}
+
 extern "C" int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, int mat,
                                      const void* A, int R, int K, int N, int group_size,
                                      const int32_t* seg_start, const int32_t* seg_len,
                                      int max_rows_per_expert, void* C, void* workspace,
                                      size_t workspace_bytes, int32_t* err, lr_stream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (!device_table || E < 1 || E > kMaxGemmExperts) return LR_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(device_table) & 127u) != 0) return LR_ERR_INVALID_ARGUMENT;
   if (mode < LR_FFN_MODE_PLAIN || mode > LR_FFN_MODE_SWIGLU) return LR_ERR_INVALID_ARGUMENT;
@@ -652,8 +657,15 @@ extern "C" int lr_grouped_w4a16_gemm(const void* device_table, int E, int mode, 
   // goes through TMA when its rows are 16-byte aligned (K % 8 == 0).
   const bool tma = N % 32 == 0 && K % 8 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
   const bool pow2_group = g >= 16 && (g & (g - 1)) == 0;
-  const int path = (tma && K % kBK == 0 && g % kBK == 0) ? 0 : (tma && pow2_group) ? 1 : 2;
+  int path = (tma && K % kBK == 0 && g % kBK == 0) ? 0 : (tma && pow2_group) ? 1 : 2;
+  // short segments with a token-term workspace: 8-bit operands
+  if (path == 0 && i8_eligible(K, N, g, mr) && workspace &&
+      (reinterpret_cast<uintptr_t>(workspace) & 127u) == 0 &&
+      workspace_bytes >= i8_workspace_bytes(R, K))
+    path = 3;
 #define LR_GEMM_MODE(M_)                                                                       \
+  if (path == 3) return launch_i8<M_>(A, K, R, tab, E, mat, N, g, seg_start, seg_len, mr, Cp,   \
+                                      workspace, err, stream);                                \
   if (path == 0) return dispatch_shape<M_>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp, \
                                            err, stream);                                      \
   if (path == 1) return launch_skinny<M_>(A, K, R, tab, E, mat, N, seg_start, seg_len, mr, Cp,  \

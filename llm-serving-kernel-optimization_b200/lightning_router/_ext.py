@@ -29,7 +29,8 @@ C_ABI_SYMBOLS = (
     "lr_dispatch_workspace_bytes", "lr_expert_routing_forward",
     "lr_combine", "lr_gather_workspace_bytes", "lr_expert_routing_gather",
     "lr_weight_table_bytes", "lr_encode_weight_table",
-    "lr_grouped_gemm_workspace_bytes", "lr_grouped_w4a16_gemm", "lr_quantized_matmul",
+    "lr_grouped_gemm_workspace_bytes", "lr_grouped_w4a16_workspace_bytes",
+    "lr_grouped_w4a16_gemm", "lr_quantized_matmul",
     "lr_ep_plan_size", "lr_ep_plan", "lr_ep_plan_tokens", "lr_ep_publish", "lr_ep_plan_wait",
     "lr_ep_signal", "lr_ep_gather", "lr_ep_combine",
     "lr_ipc_export", "lr_ipc_import", "lr_ipc_close",

@@ -92,15 +92,28 @@ def clear_weight_tables() -> None:
     _TABLE_CACHE.clear()
 
 
+# Segments of at most 32 rows (decode) run on 8-bit tensor-core operands when
+# the shape allows it (K and group size multiples of 128, N % 32 == 0): token
+# rows as two 8-bit terms per 128-k block, INT4 codes as bytes (see
+# ``lr_grouped_w4a16_workspace_bytes``).  False keeps every call on the
+# fp16-operand kernels.
+INT8_OPERANDS = True
+
+
 def grouped_w4a16(table: WeightTable, num_experts: int, mode: int, mat: int, A: torch.Tensor,
                   N: int, seg_start: torch.Tensor | None, seg_len: torch.Tensor | None,
-                  max_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Grouped GEMM over expert row segments; see ``lr_grouped_w4a16_gemm``."""
+                  max_rows: int, out: torch.Tensor | None = None,
+                  int8_operands: bool | None = None) -> torch.Tensor:
+    """Grouped GEMM over expert row segments; see ``lr_grouped_w4a16_gemm``.
+
+    ``int8_operands`` (default :data:`INT8_OPERANDS`) lets short segments take
+    the 8-bit operand kernel."""
     _ext.require_cuda(A)
     err = _ext.error_word(A.device.index)
+    i8 = INT8_OPERANDS if int8_operands is None else bool(int8_operands)
     return _ext.ops().grouped_w4a16_gemm(table.table, int(num_experts), int(mode), int(mat),
                                          A.contiguous(), int(N), table.group_size, seg_start,
-                                         seg_len, int(max_rows), out, err)
+                                         seg_len, int(max_rows), out, err, i8)
 
 
 def quantized_matmul(

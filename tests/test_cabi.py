@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = _ext.clib()
-    assert lib.lr_abi_version() == 2
+    assert lib.lr_abi_version() == 3
     assert lib.lr_status_string(0) == b"ok"
     assert b"invalid" in lib.lr_status_string(-1)
     assert b"workspace" in lib.lr_status_string(-4)
@@ -51,6 +51,29 @@ def test_workspace_queries_are_host_only():
     assert small >= 256 + 8 * 64 * 8 * 4 + 64 * 2 * 4
     assert small >= lib.lr_route_workspace_bytes(64, 2, 8)
     assert lib.lr_gate_dispatch_workspace_bytes(4096, 2, 8) == lib.lr_route_workspace_bytes(4096, 2, 8)
+
+
+def test_int8_operand_workspace_query():
+    """The 8-bit GEMM path's workspace: two 8-bit terms per token element plus a
+    (sigma, block sum) pair per row and 128-k block; zero for shapes it does not take."""
+    lib = _ext.clib()
+    f = lib.lr_grouped_w4a16_workspace_bytes
+    f.restype = ctypes.c_size_t
+
+    def a128(b):
+        return (b + 127) // 128 * 128
+
+    # decode Mixtral-shaped gate/up: R = 128 rows, K = 4096, N = 14336, capacity 20
+    assert f(8, 128, 4096, 14336, 128, 20) == a128(2 * 128 * 4096) + 2 * a128(4 * 128 * 32)
+    assert f(8, 128, 14336, 4096, 128, 20) == a128(2 * 128 * 14336) + 2 * a128(4 * 128 * 112)
+    assert f(1, 5, 256, 64, 256, 5) == a128(2 * 5 * 256) + 2 * a128(4 * 5 * 2)
+    for args in [(8, 128, 4096, 14336, 128, 33),   # segments longer than 32 rows
+                 (8, 128, 4096, 14336, 64, 20),    # group size not a multiple of 128
+                 (8, 128, 4160, 14336, 64, 20),    # K not a multiple of 128
+                 (8, 128, 4096, 14344, 128, 20),   # N not a multiple of 32
+                 (8, 128, 4096, 14336, 128, 0), (0, 128, 4096, 14336, 128, 20),
+                 (8, 0, 4096, 14336, 128, 20), (8, 128, 4096, 14336, 100, 20)]:
+        assert f(*args) == 0, args
 
 
 def test_argument_validation_without_device():

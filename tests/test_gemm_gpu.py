@@ -299,3 +299,94 @@ def test_expert_rows_independent_of_other_experts(mode, d, lens):
         torch.nn.functional.silu(x @ deq[0].float()) * (x @ deq[1].float())
     _check(out1[:L0], ref)
 
+
+
+def _ref_mode(x, de, mode):
+    if mode == 0:
+        return x @ de[1].float()
+    if mode == 1:
+        return torch.nn.functional.silu(x @ de[1].float())
+    return torch.nn.functional.silu(x @ de[0].float()) * (x @ de[1].float())
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("d,f,g,lens", [
+    (1024, 2048, 128, [20, 0, 32, 7, 1]),
+    (4096, 1024, 128, [16, 16, 3, 0]),
+    (1024, 1152, 128, [32, 5]),          # 1152 output rows: a partial 256-row weight tile
+    (2048, 1024, 256, [31, 1, 12]),      # one group spans two 128-k blocks
+])
+def test_int8_operand_path(mode, d, f, g, lens):
+    """Segments of at most 32 rows with K and the group size multiples of 128 run on
+    8-bit operands (token rows as two 8-bit terms per 128-k block, INT4 codes as
+    bytes, scale and zero folded per block).  Checked against the fp32 reference
+    at the same bar as every GEMM, against the fp16-operand kernel on the same
+    inputs, for repeat determinism, and rows outside the segments stay unwritten."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E = len(lens)
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, mode, seed=d + f + g + mode)
+    maxr = max(lens)
+    sentinel = torch.full((R, f), 3.0, dtype=torch.float16, device=DEV)
+    out = grouped_w4a16(table, E, mode, 1, A, f, ss, sl, maxr, out=sentinel.clone())
+    again = grouped_w4a16(table, E, mode, 1, A, f, ss, sl, maxr, out=sentinel.clone())
+    f16 = grouped_w4a16(table, E, mode, 1, A, f, ss, sl, maxr, int8_operands=False)
+    assert torch.equal(out, again)
+    covered = torch.zeros(R, dtype=torch.bool, device=DEV)
+    for e, L in enumerate(lens):
+        st = int(ss[e])
+        if L == 0:
+            continue
+        ref = _ref_mode(A[st:st + L].float(), deq[e], mode)
+        _check(out[st:st + L], ref)
+        _check(f16[st:st + L], ref)
+        _check(out[st:st + L], f16[st:st + L].float())
+        covered[st:st + L] = True
+    assert torch.equal(out[~covered], sentinel[~covered])
+
+
+def test_int8_operand_path_rows_independent_of_other_experts():
+    """On the 8-bit path an expert's rows are bit-identical alone or among 8 experts:
+    each row's terms and its block sums depend on that row only."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16, weight_table
+    E, d, f, g = 8, 1024, 2048, 128
+    lens = [20, 7, 31, 12, 1, 30, 0, 25]
+    q, s, z, deq = [], [], [], []
+    for e in range(E):
+        for m, (K, N) in enumerate([(d, f), (d, f), (f, d)]):
+            qw, sc, zr, Wd = _quant(K, N, g, 700 + e * 3 + m)
+            q.append(qw), s.append(sc), z.append(zr)
+            if e == 0:
+                deq.append(Wd)
+    starts = [0]
+    for L in lens[:-1]:
+        starts.append(starts[-1] + L)
+    R = starts[-1] + lens[-1]
+    A = torch.randn(R, d, generator=torch.Generator().manual_seed(5)).half().to(DEV)
+    ss = torch.tensor(starts, dtype=torch.int32, device=DEV)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    table8 = weight_table(q, s, z, E, d, f, g, True)
+    table1 = weight_table(q[:3], s[:3], z[:3], 1, d, f, g, True)
+    L0 = lens[0]
+    for mode in (0, 2):
+        out8 = grouped_w4a16(table8, E, mode, 1, A, f, ss, sl, max(lens))
+        out1 = grouped_w4a16(table1, 1, mode, 1, A[:L0].contiguous(), f, ss[:1], sl[:1], L0)
+        assert torch.equal(out8[:L0], out1[:L0])
+        _check(out1[:L0], _ref_mode(A[:L0].float(), deq, mode))
+
+
+def test_int8_operand_path_large_rows_and_zero_rows():
+    """Rows of large magnitude, all-zero rows and rows with a single non-zero entry
+    per block keep the bar (the terms scale with each block's maximum)."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E, d, f, g = 2, 1024, 1024, 128
+    lens = [24, 9]
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, 0, seed=11)
+    A[0:4] *= 200.0
+    A[4:6] = 0
+    A[6:8] = 0
+    A[6:8, ::128] = 1.5
+    out = grouped_w4a16(table, E, 0, 1, A, f, ss, sl, max(lens))
+    for e, L in enumerate(lens):
+        st = int(ss[e])
+        _check(out[st:st + L], A[st:st + L].float() @ deq[e][1].float())
+    assert torch.equal(out[4:6], torch.zeros_like(out[4:6]))
