@@ -59,11 +59,12 @@ UNIT = "tokens/s"
 #       --clock-control none --profile-from-start off \
 #       python bench.py [--workload decode] --steps 2 --warmup 3 --no-cpu
 # prefill: 980.4 MB read (algorithmic 757: token rows 268 + weights 489) and 911.4 MB
-# written (940 of intermediate rows, part still in L2 at the end); decode: 489.8 MB
-# read (the weights of the 8 experts), 2.7 MB written.
+# written (940 of intermediate rows, part still in L2 at the end); decode (the stage is
+# the token-term pass and the 8-bit-operand GEMM): 1.1 + 489.7 MB read (the weights of
+# the 8 experts), 2.7 MB written.
 NCU_TRAFFIC = {
     "prefill": 980.4e6 + 911.4e6,
-    "decode": 489.8e6 + 2.7e6,
+    "decode": 1.1e6 + 489.7e6 + 2.7e6,
 }
 
 
