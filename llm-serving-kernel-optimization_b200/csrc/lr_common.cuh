@@ -47,12 +47,46 @@ inline int set_dyn_smem_once(Kernel kern, int bytes, unsigned long long& done,
   return 0;
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// before its predecessor in the stream has finished, hiding the launch latency
+// between the short kernels of a decode step.  Every kernel launched this way
+// calls pdl_wait() before its first global-memory access, so it neither reads
+// the predecessor's outputs nor overwrites memory the predecessor still reads
+// before the predecessor has completed.  Inside a stream capture the attribute
+// is left off: a graph's launches are prepared already, and programmatic edges
+// measured slower there (decode step 0.335 against 0.329 ms; eager 0.341
+// against 0.347 ms with the attribute).
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusNone;
+  cfg.numAttrs = cs == cudaStreamCaptureStatusNone ? 1 : 0;
+  LR_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+  return 0;
+}
+
 // ---------------------------------------------------------------------------
 // device error word
 // ---------------------------------------------------------------------------
 LR_DEVICE void report(int32_t* err, int bits) {
   if (err) atomicOr(reinterpret_cast<int*>(err), bits);
 }
+
+// Wait until the predecessor grid in the stream has completed and its memory
+// operations are visible (a no-op without programmatic serialization).
+LR_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the successor grid to be scheduled (it still waits in pdl_wait()).
+LR_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 LR_DEVICE uint32_t lane_id() { return threadIdx.x & 31u; }
 LR_DEVICE uint32_t lanemask_lt() {

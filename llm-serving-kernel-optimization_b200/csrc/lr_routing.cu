@@ -615,6 +615,8 @@ __global__ void __launch_bounds__(kRouteThreads)
                             int32_t* __restrict__ kept_counts, float* __restrict__ aux_loss,
                             float* __restrict__ routing_w, int32_t* __restrict__ src_idx,
                             int32_t* __restrict__ slot_pos, SmallRouteWs ws, int num_blocks) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) __half s_gate[];  // [kSgTok][kSgLd] tokens, [Epad][kSgLd] gate
   __shared__ int32_t s_ids[kRouteThreads * kMaxTopK];
   __shared__ int32_t s_rank[kRouteThreads * kMaxTopK];
@@ -771,6 +773,8 @@ __global__ void __launch_bounds__(256)
     permute_rows_kernel(const uint4* __restrict__ x, int T, int d8, int k, int parts, int fill,
                         const int32_t* __restrict__ slot_pos,
                         const int32_t* __restrict__ slot_row, uint4* __restrict__ permuted) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int t = gw / parts, part = gw % parts;
   if (t >= T) return;
@@ -804,6 +808,8 @@ __global__ void __launch_bounds__(256)
     combine_kernel(const uint4* __restrict__ y, const float* __restrict__ gate_w,
                    const int32_t* __restrict__ slot_pos, int T, int k, int d8, int parts,
                    uint4* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int t = gw / parts, part = gw % parts;
   if (t >= T) return;
@@ -1090,11 +1096,12 @@ static int launch_gate_route_small(const void* x, const void* wg, const float* b
   static unsigned long long configured = 0;
   if (const int rc = set_dyn_smem_once(kern, int(small_gate_smem_bytes(64)), configured)) return rc;
   const int blocks = kGateWarps * ((T + kSgTok - 1) / kSgTok);
-  kern<<<blocks, kRouteThreads, small_gate_smem_bytes(E), stream>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(wg), bias, T, d, E, k, capacity,
-      lbw, logits, expert_ids, gate_weights, token_indices, offsets, kept_counts, aux_loss,
-      routing_w, source_idx, slot_pos, ws, blocks);
-  LR_LAUNCH_CHECK();
+  if (const int rc = launch_pdl(kern, dim3(blocks), dim3(kRouteThreads), small_gate_smem_bytes(E),
+                               stream, static_cast<const __half*>(x),
+                               static_cast<const __half*>(wg), bias, T, d, E, k, capacity, lbw,
+                               logits, expert_ids, gate_weights, token_indices, offsets,
+                               kept_counts, aux_loss, routing_w, source_idx, slot_pos, ws, blocks))
+    return rc;
   return LR_OK;
 }
 
@@ -1141,10 +1148,11 @@ extern "C" int lr_gate_topk_gating_dispatch(
 #undef LR_SMALL_CASE
   if (rc != LR_OK || permuted == nullptr) return rc;
   const int parts = row_parts(T, d / 8);
-  permute_rows_kernel<<<unsigned((long(T) * parts + 7) / 8), 256, 0, stream>>>(
-      static_cast<const uint4*>(x), T, d / 8, k, parts, fill_dropped, slot_pos, ws.slot_row,
-      static_cast<uint4*>(permuted));
-  LR_LAUNCH_CHECK();
+  if (const int rc = launch_pdl(permute_rows_kernel, dim3(unsigned((long(T) * parts + 7) / 8)),
+                               dim3(256), 0, stream, static_cast<const uint4*>(x), T, d / 8, k,
+                               parts, fill_dropped, slot_pos, ws.slot_row,
+                               static_cast<uint4*>(permuted)))
+    return rc;
   return LR_OK;
 }
 
@@ -1198,10 +1206,10 @@ extern "C" int lr_combine(const void* y, const float* gate_weights, const int32_
   if (!y || !gate_weights || !slot_pos || !out || !aligned16(y) || !aligned16(out))
     return LR_ERR_INVALID_ARGUMENT;
   const int parts = row_parts(T, d / 8);
-  combine_kernel<<<unsigned((long(T) * parts + 7) / 8), 256, 0, stream>>>(
-      static_cast<const uint4*>(y), gate_weights, slot_pos, T, k, d / 8, parts,
-      static_cast<uint4*>(out));
-  LR_LAUNCH_CHECK();
+  if (const int rc = launch_pdl(combine_kernel, dim3(unsigned((long(T) * parts + 7) / 8)),
+                               dim3(256), 0, stream, static_cast<const uint4*>(y), gate_weights,
+                               slot_pos, T, k, d / 8, parts, static_cast<uint4*>(out)))
+    return rc;
   return LR_OK;
 }
 

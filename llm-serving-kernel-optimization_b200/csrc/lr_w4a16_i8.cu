@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(256)
     quantize_rows_i8x2_kernel(const __half* __restrict__ A, int R, int K,
                               int8_t* __restrict__ Aq, float* __restrict__ sig,
                               int32_t* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
   const int KB = K / i8::kQK;
   const int lane = threadIdx.x & 31;
   const long total = long(R) * KB;
@@ -283,8 +285,12 @@ __global__ void __launch_bounds__(i8::kThreads, 1)
     tmem_alloc(s_tmem, kTmemCols);
     tmem_relinquish();
   }
+  if (warp == kTokWarp && lane == 0) tma_prefetch_desc(&tmap_q);
+  // everything above touches only shared and tensor memory; the segments, token
+  // terms and parameters below are the predecessors' outputs
+  pdl_wait();
+  pdl_trigger();
   if (warp == kTokWarp) {
-    if (lane == 0) tma_prefetch_desc(&tmap_q);
     build_tile_table(seg_start, seg_len, E, R, max_rows, kRows, n_tiles, s_tbase, s_start, s_len,
                      s_mt, err);
   }
@@ -742,9 +748,9 @@ int launch_i8(const void* A, int K, int R, const ExpertEntry* table, int E, int 
     const long warps = long(R) * KB;
     long blocks = (warps + 7) / 8;
     if (blocks > long(sms) * 16) blocks = long(sms) * 16;
-    quantize_rows_i8x2_kernel<<<unsigned(blocks), 256, 0, stream>>>(
-        static_cast<const __half*>(A), R, K, q, sig, xs);
-    LR_LAUNCH_CHECK();
+    if (const int rc = launch_pdl(quantize_rows_i8x2_kernel, dim3(unsigned(blocks)), dim3(256), 0,
+                                  stream, static_cast<const __half*>(A), R, K, q, sig, xs))
+      return rc;
   }
   auto kern = w4a16_i8_gemm_kernel<MODE>;
   static unsigned long long configured = 0;
@@ -755,9 +761,11 @@ int launch_i8(const void* A, int K, int R, const ExpertEntry* table, int E, int 
   const long n_tiles = (N + BO - 1) / BO;
   const long upper = long(E) * ((max_rows + i8::kRows - 1) / i8::kRows) * n_tiles;
   const int grid = int(upper < sms ? (upper < 1 ? 1 : upper) : sms);
-  kern<<<grid, i8::kThreads, i8::kTotal, stream>>>(tq, table, E, mat, K, N, group_size, seg_start,
-                                                   seg_len, max_rows, R, sig, xs, C, err);
-  LR_LAUNCH_CHECK();
+  if (const int rc = launch_pdl(kern, dim3(grid), dim3(i8::kThreads), size_t(i8::kTotal), stream,
+                               tq, table, E, mat, K, N, group_size, seg_start, seg_len, max_rows,
+                               R, static_cast<const float*>(sig), static_cast<const int32_t*>(xs),
+                               C, err))
+    return rc;
   return LR_OK;
 }
 
