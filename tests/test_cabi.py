@@ -30,6 +30,17 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
 
 
+def test_torch_op_library_loads_and_registers_every_op():
+    """The torch-op shim loads without a GPU (its op schemas parse at load time)."""
+    ops = _ext.ops()
+    for name in ("gate_logits", "topk_gating_dispatch", "gate_topk_gating_dispatch",
+                 "expert_routing_forward", "combine", "topk_route", "permute_tokens",
+                 "expert_routing_gather", "encode_weight_table", "grouped_w4a16_gemm",
+                 "route_rows", "ep_plan", "ep_plan_tokens", "ep_gather", "ep_combine",
+                 "ep_publish", "ep_plan_wait", "ep_signal"):
+        assert hasattr(ops, name), name
+
+
 def test_status_strings_and_version():
     lib = _ext.clib()
     assert lib.lr_abi_version() == 3
