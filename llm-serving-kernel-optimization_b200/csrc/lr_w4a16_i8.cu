@@ -3,8 +3,9 @@
 //
 // At decode an expert sees at most a few dozen token rows, so the GEMM is a
 // stream of packed INT4 weights.  With fp16 operands every weight is written to
-// and read from shared memory as two bytes, and that traffic, not HBM, bounds
-// the weight stream.  This kernel feeds the tensor core 8-bit operands instead:
+// and read from shared memory as two bytes and the tensor core spends a whole
+// instruction on each 16-deep slice.  This kernel feeds the tensor core 8-bit
+// operands instead (half the operand bytes, twice the depth per instruction):
 //
 //   weights  the INT4 codes q in [0, 15] themselves, as unsigned bytes (exact).
 //            Unpacking a packed word is two masks and a shift: the low nibbles
