@@ -390,3 +390,25 @@ def test_int8_operand_path_large_rows_and_zero_rows():
         st = int(ss[e])
         _check(out[st:st + L], A[st:st + L].float() @ deq[e][1].float())
     assert torch.equal(out[4:6], torch.zeros_like(out[4:6]))
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+def test_int8_operand_path_one_block_and_many_experts(mode):
+    """K = 128 (one 128-deep block per tile for gate/up) with 64 experts of 0-32 rows:
+    many tiles per CTA, empty experts between full ones, and a 64-entry tile table."""
+    from lightning_router.kernels.quantized_matmul import grouped_w4a16
+    E, d, f, g = 64, 128, 256, 128
+    gen = torch.Generator().manual_seed(21)
+    lens = [int(x) for x in torch.randint(0, 33, (E,), generator=gen)]
+    lens[0], lens[5], lens[63] = 32, 0, 1
+    table, A, ss, sl, deq, R = _grouped_case(E, d, f, g, lens, mode, seed=31 + mode)
+    sentinel = torch.full((R, f), 9.0, dtype=torch.float16, device=DEV)
+    out = grouped_w4a16(table, E, mode, 1, A, f, ss, sl, 32, out=sentinel.clone())
+    covered = torch.zeros(R, dtype=torch.bool, device=DEV)
+    for e, L in enumerate(lens):
+        if L == 0:
+            continue
+        st = int(ss[e])
+        _check(out[st:st + L], _ref_mode(A[st:st + L].float(), deq[e], mode))
+        covered[st:st + L] = True
+    assert torch.equal(out[~covered], sentinel[~covered])
