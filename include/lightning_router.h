@@ -215,7 +215,7 @@ size_t lr_grouped_gemm_workspace_bytes(int num_experts);
  * K % 128 == 0, group_size % 128 == 0 and N % 32 == 0 (decode).  There the
  * token rows are written as two signed 8-bit terms per 128-k block
  * (x ~ sigma * (a1 + a2/256), sigma = max|x|/127 of the block; error at most
- * sigma/512) and the INT4 codes enter the tensor core as unsigned bytes; the
+ * sigma/512, sigma/256 where the second term saturates) and the INT4 codes enter the tensor core as unsigned bytes; the
  * group scale and zero are applied in fp32 per 128-k block.  Returns 0 for
  * shapes that do not take that path.  Without the workspace the same call
  * runs the fp16-operand kernel.                                               */

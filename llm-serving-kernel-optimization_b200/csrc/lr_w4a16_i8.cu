@@ -14,7 +14,8 @@
 //            x ~= sigma * (a1 + a2 / 256) with sigma = max|x| / 127 of the block,
 //            a1 = round(x / sigma), a2 = round(256 * (x - sigma * a1) / sigma).
 //            The reconstruction error is at most sigma / 512 per element (16-bit
-//            fixed point relative to the block maximum).
+//            fixed point relative to the block maximum), or sigma / 256 where the
+//            residual sits at +-sigma / 2 and a2 saturates at +-127.
 //
 // The weights are the UMMA A operand (M = 128 weight rows, MN-major), the two
 // token terms of up to 32 rows the B operand (N = 64, K-major).  The group
