@@ -86,3 +86,34 @@ def test_fold_equals_terms_times_dequant_and_meets_tolerance(K, N, g):
     rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
     assert rel <= 1e-3, rel
     assert np.abs(y - ref).max() <= 2e-2 * np.abs(ref).max()
+
+
+def test_unpacked_byte_order_and_its_inverse():
+    """Two packed words (16 features of one k) unpacked as the weight-operand
+    warps do -- low nibbles of word 0, its high nibbles, then word 1 -- put
+    feature chunk_feature(b) at byte b; the epilogue maps TMEM lane b back
+    with that function (pack_weights.py: nibble i of word j is column 8j+i)."""
+    import torch
+    import lightning_router.quantization.pack_weights as pw
+
+    rng = np.random.default_rng(7)
+    q = torch.from_numpy(rng.integers(0, 16, (3, 64)).astype(np.int32))
+    words = pw._pack_int4(q).numpy().view(np.uint32)          # [3, 8]
+
+    def unpack(w):
+        out = []
+        for v in (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F):
+            out += [(int(v) >> (8 * i)) & 0xFF for i in range(4)]
+        return out
+
+    def chunk_feature(b):
+        return (b & 8) | ((b & 3) << 1) | ((b >> 2) & 1)
+
+    assert sorted(chunk_feature(b) for b in range(16)) == list(range(16))
+    assert [chunk_feature(b) for b in range(16)] == [0, 2, 4, 6, 1, 3, 5, 7,
+                                                     8, 10, 12, 14, 9, 11, 13, 15]
+    for k in range(3):
+        for c in range(4):                                     # 16-feature chunks
+            got = unpack(words[k, 2 * c]) + unpack(words[k, 2 * c + 1])
+            for b in range(16):
+                assert got[b] == int(q[k, 16 * c + chunk_feature(b)])
